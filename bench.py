@@ -1,0 +1,380 @@
+"""Benchmark of the MxWave hot path on B200 (one JSON line on rank 0).
+
+Workload (one step): gamma-weighted MXFP4 quantization of an MLP up/gate
+pair -- per-channel second moments of 8192 x 5120 bf16 calibration
+activations (heavy-channel law) -> rms -> quantize two 17408 x 5120 bf16
+weights (N(0, 0.015^2)) with the rms-weighted block error, percentile 99.5,
+clip depth 1 (the reference defaults).  Inputs are synthetic (no checkpoint
+offline) and larger than L2 (356 MB of weights per step).
+
+``value`` is the whole-job rate of bf16 weight bytes quantized (GB/s) with
+inputs resident in HBM; ``e2e`` is the same rate through the public Python
+API from pinned host memory (H2D of weights + activations, D2H of packed
+bytes and scales inside the timed region).  With --gpus N (torchrun) every
+rank quantizes its own weights (row/tensor sharding, no communication) and
+the time is the max over ranks.
+
+``--impl reference`` times the CPU restatement of the reference's algorithm
+(oracle port, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+TOKENS, HIDDEN, INTER = 8192, 5120, 17408
+N_WEIGHTS = 2
+DEPTH = 1
+PCT = 99.5
+BYTES_PER_ELEM = 2 + 0.5 + 1.0 / 32  # bf16 in, nibbles + E8M0 out
+WORKLOAD = (
+    f"gamma-weighted MXFP4 quantize of MLP up/gate {N_WEIGHTS}x{INTER}x{HIDDEN} bf16 "
+    f"(rms from {TOKENS}x{HIDDEN} bf16 activations), pct {PCT}, depth {DEPTH}"
+)
+METRIC = "bf16 weight GB/s quantized"
+
+
+def _peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (getattr(self, "out", "") or "").splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(smax), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ our arm
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from mxwave_b200 import _lib, synthetic
+    from mxwave_b200.core import quantize_mxfp4
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+
+    x = synthetic.torch_activations(TOKENS, HIDDEN, seed=2 + 1000 * rank, device=dev)
+    ws = [synthetic.torch_dense_weight(INTER, HIDDEN, seed=20 + i + 1000 * rank, device=dev, sigma=0.015,
+                                       outlier_fraction=0.0) for i in range(N_WEIGHTS)]
+    sum_sq = torch.zeros(HIDDEN, device=dev)
+    rms = torch.empty(HIDDEN, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    elems = N_WEIGHTS * INTER * HIDDEN
+    ev_q = []
+
+    def step(record: bool) -> list:
+        sum_sq.zero_()
+        _lib.check(lib.mxw_accumulate_moments(x.data_ptr(), _lib.MXW_BF16, TOKENS, HIDDEN, HIDDEN, None,
+                                              sum_sq.data_ptr(), stream.cuda_stream), "moments")
+        _lib.check(lib.mxw_finalize_moments(None, sum_sq.data_ptr(), HIDDEN, TOKENS, None, rms.data_ptr(),
+                                            stream.cuda_stream), "finalize")
+        outs = []
+        for w in ws:
+            if record:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+            outs.append(quantize_mxfp4(w, scale_percentile=PCT, gamma=rms, mse_clip_depth=DEPTH))
+            if record:
+                b.record(stream)
+                ev_q.append((a, b))
+        return outs
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        time.sleep(0.3)
+        start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        stop.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    q_ms = sum(a.elapsed_time(b) for a, b in ev_q) / len(ev_q)
+
+    # ---- end to end through the public API, host pinned buffers.
+    e2e = run_e2e(args, dev, world, rank)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = _peaks()
+    bytes_per_launch = INTER * HIDDEN * BYTES_PER_ELEM + HIDDEN * 4
+    achieved = bytes_per_launch / (q_ms * 1e-3) / 1e9
+    value = world * elems * 2 * args.steps / (ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (bf16 in, u8 out)",
+        "data": "synthetic (seeded on-device normal weights, heavy-channel activations)",
+        "config": {"workload": WORKLOAD, "elements_per_step_per_gpu": elems, "l2": "inputs > L2 (356 MB weights)",
+                   "parallelism": f"tensor-sharded x{world}, no collective"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
+                     "traffic": args.traffic, "kernel": "quantize_tma_kernel<bf16,gamma,top2>",
+                     "bytes_per_launch": int(bytes_per_launch), "avg_launch_ms": round(q_ms, 4)},
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, dev, world: int, rank: int) -> dict:
+    """Same step through the public API with pinned host inputs and outputs."""
+    import torch
+
+    from mxwave_b200 import synthetic
+    from mxwave_b200.calibration import ActivationCollector
+    from mxwave_b200.core import quantize_mxfp4
+
+    x_h = synthetic.torch_activations(TOKENS, HIDDEN, seed=7 + rank, device=dev).cpu().pin_memory()
+    w_h = [synthetic.torch_dense_weight(INTER, HIDDEN, seed=70 + i + rank, device=dev, sigma=0.015,
+                                        outlier_fraction=0.0).cpu().pin_memory() for i in range(N_WEIGHTS)]
+    p_h = [torch.empty((INTER, HIDDEN // 2), dtype=torch.uint8).pin_memory() for _ in range(N_WEIGHTS)]
+    s_h = [torch.empty((INTER, HIDDEN // 32), dtype=torch.uint8).pin_memory() for _ in range(N_WEIGHTS)]
+    stream = torch.cuda.current_stream(dev)
+
+    def step() -> None:
+        col = ActivationCollector({"mlp.weight": HIDDEN}, ("rms",))
+        col.update("mlp.weight", x_h.to(dev, non_blocking=True))
+        rms = col.finalize_on_device()["rms"]["mlp.weight"]
+        for i, w in enumerate(w_h):
+            p, s = quantize_mxfp4(w.to(dev, non_blocking=True), scale_percentile=PCT, gamma=rms,
+                                  mse_clip_depth=DEPTH)
+            p_h[i].copy_(p, non_blocking=True)
+            s_h[i].copy_(s, non_blocking=True)
+
+    for _ in range(max(2, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(2, args.steps // 2)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    elems = N_WEIGHTS * INTER * HIDDEN
+    return {
+        "value": round(world * elems * 2 * steps / (ms * 1e-3) / 1e9, 3),
+        "unit": "GB/s",
+        "h2d_bytes_per_step": int(elems * 2 + TOKENS * HIDDEN * 2),
+        "d2h_bytes_per_step": int(elems // 2 + elems // 32),
+        "ms_per_step": round(ms / steps, 3),
+    }
+
+
+# ---------------------------------------------------------- CPU reference
+
+
+def _oracle_sample(rows: int):
+    """A row sample of the workload for the CPU restatement (numpy inputs)."""
+    import numpy as np
+
+    from mxwave_b200 import synthetic
+
+    x = synthetic.bf16_bits_to_f32(synthetic.det_activations(1024, HIDDEN, seed=2)).astype(np.float64)
+    gamma = np.sqrt((x * x).mean(0)).astype(np.float32)
+    ws = [synthetic.det_dense_weight(rows, HIDDEN, seed=20 + i, sigma=0.015, outlier_fraction=0.0)
+          for i in range(N_WEIGHTS)]
+    return ws, gamma
+
+
+def cpu_baseline(seconds: float) -> dict:
+    """Time the oracle port of the reference algorithm on the host cores."""
+    from oracle import oracle
+
+    threads = oracle.default_threads()
+    ws, gamma = _oracle_sample(256)
+    t0 = time.perf_counter()
+    for w in ws:
+        oracle.quantize_mxfp4(w, PCT, gamma=gamma, mse_clip_depth=DEPTH, threads=threads)
+    probe = time.perf_counter() - t0
+    rows = int(max(64, min(INTER, 256 * seconds / max(probe, 1e-3))))
+    ws, gamma = _oracle_sample(rows)
+    t0 = time.perf_counter()
+    for w in ws:
+        oracle.quantize_mxfp4(w, PCT, gamma=gamma, mse_clip_depth=DEPTH, threads=threads)
+    dt = time.perf_counter() - t0
+    elems = N_WEIGHTS * rows * HIDDEN
+    return {"value": round(elems * 2 / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{N_WEIGHTS} x {rows} rows x {HIDDEN} of the workload's weights ({dt:.1f} s)"}
+
+
+def run_reference(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    threads = oracle.default_threads()
+    ws, gamma = _oracle_sample(256)
+    t0 = time.perf_counter()
+    oracle.quantize_mxfp4(ws[0], PCT, gamma=gamma, mse_clip_depth=DEPTH, threads=threads)
+    probe = time.perf_counter() - t0
+    # Each step quantizes a bounded row sample of both weights (~1.5 s of CPU work).
+    rows = int(max(32, min(INTER, 128 * 1.5 / max(probe, 1e-3))))
+    ws, gamma = _oracle_sample(rows)
+
+    def step() -> None:
+        for w in ws:
+            oracle.quantize_mxfp4(w, PCT, gamma=gamma, mse_clip_depth=DEPTH, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    elems = N_WEIGHTS * rows * HIDDEN
+    value = elems * 2 * args.steps / dt / 1e9
+    sample = f"{N_WEIGHTS} x {rows} rows x {HIDDEN} per step of the workload's weights"
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (bf16 in, u8 out)",
+        "data": "synthetic (seeded, platform-independent generator)",
+        "config": {"workload": WORKLOAD, "sample": sample},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="dram bytes per quantize launch from an ncu capture (recorded in the roofline)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,143 @@
+/*
+ * mxwave_b200 -- C ABI of the B200 (sm_100a) MxWave hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as `void*` (NULL = the legacy default stream), launches asynchronously
+ * on that stream, allocates nothing, and returns an mxw_status code.  Argument
+ * errors are detected on the host before any launch.  Kernels never trap; a
+ * data-dependent failure (a NaN/inf weight) is reported through a caller-owned
+ * device flag word that the caller reads when it next synchronises.
+ *
+ * Layouts follow the reference exactly:
+ *   weight  [rows, cols] row-major, row stride `ld` elements (bf16/f16/f32)
+ *   packed  [rows, cols/2] uint8, element 2j in the low nibble of byte j
+ *   scales  [rows, cols/32] uint8, E8M0 biased exponent (exponent + 127)
+ *   gamma   [cols] fp32;  hessian [cols/32, 32, 32] fp32
+ * (compressed-tensors "mxfp4-pack-quantized", mxwave/core.py:147-149, 249-251)
+ */
+#ifndef MXWAVE_B200_H_
+#define MXWAVE_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MXW_API __attribute__((visibility("default")))
+#else
+#define MXW_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MXW_OK 0
+#define MXW_EINVAL 1      /* bad argument (detected before launch)            */
+#define MXW_ENONFINITE 2  /* reserved for callers mapping the flag word       */
+#define MXW_ECUDA 3       /* a CUDA runtime call failed (see mxw_last_cuda_error) */
+#define MXW_ETIMEOUT 4    /* a bounded device wait gave up                    */
+#define MXW_EUNSUPPORTED 5
+
+/* Element types of weight / activation inputs. */
+#define MXW_BF16 0
+#define MXW_F16 1
+#define MXW_F32 2
+
+/* Scale-selection methods (mxwave/core.py:22). */
+#define MXW_METHOD_MSE 0
+#define MXW_METHOD_RTN 1
+
+/* Hessian damping modes (mxwave/core.py:23). */
+#define MXW_DAMP_ABSOLUTE 0
+#define MXW_DAMP_RELATIVE 1
+
+/* Bits of the device flag word written by the kernels. */
+#define MXW_FLAG_NONFINITE 1 /* the input held a NaN or infinity                 */
+#define MXW_FLAG_TIMEOUT 2   /* a bounded on-device wait gave up; output invalid */
+
+/* Human-readable name of a status code. */
+MXW_API const char* mxw_status_string(int status);
+
+/* The cudaError_t of the last MXW_ECUDA returned on this host thread. */
+MXW_API int mxw_last_cuda_error(void);
+
+/* Library version string. */
+MXW_API const char* mxw_version(void);
+
+/*
+ * MXFP4 quantization of one row slice.
+ * Replaces mxwave.core.quantize_mxfp4 (mxwave/core.py:114-251): percentile or
+ * amax anchor, the explicit exponent candidate set floor-depth .. floor+1 plus
+ * the no-clipping exponent, unweighted / gamma^2-weighted / block-Hessian
+ * error, strict-< argmin (earliest candidate wins ties), E2M1 round-to-nearest
+ * -even, nibble packing and E8M0 bytes.  method MXW_METHOD_RTN follows
+ * _rtn_scale_exponent (core.py:91-104).  Output bytes are identical to the
+ * reference's CPU fp32 implementation.
+ *   gamma, hessian: device pointers or NULL (mutually exclusive; MSE only).
+ *   flags: device uint32 word; MXW_FLAG_NONFINITE is OR-ed in when the slice
+ *          holds a NaN or infinity (checkpoint.py:117), or NULL to skip.
+ */
+MXW_API int mxw_quantize_mxfp4(const void* weight, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                       double scale_percentile, const float* gamma, const float* hessian,
+                       int method, int mse_clip_depth, uint8_t* packed, uint8_t* scales,
+                       uint32_t* flags, void* stream);
+
+/*
+ * Dequantize packed/scales to fp32 [rows, cols].
+ * Replaces mxwave.core.dequant_mxfp4 (mxwave/core.py:254-278).
+ */
+MXW_API int mxw_dequant_mxfp4(const uint8_t* packed, const uint8_t* scales, int64_t rows, int64_t cols,
+                      float* out, void* stream);
+
+/*
+ * Per-channel moments of activations x [tokens, cols] (row stride ld), added
+ * into sum_abs[cols] (sum |x|) and sum_sq[cols] (sum x^2); either may be NULL.
+ * Replaces the mean-abs / rms accumulation of ActivationCollector.update
+ * (mxwave/calibration.py:227-232).
+ */
+MXW_API int mxw_accumulate_moments(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ld,
+                           float* sum_abs, float* sum_sq, void* stream);
+
+/*
+ * Diagonal 32x32 blocks of X^T X added into gram_blocks [cols/32, 32, 32].
+ * Replaces the block-hessian accumulation of ActivationCollector.update
+ * (mxwave/calibration.py:233-236, einsum "nbi,nbj->bij").
+ */
+MXW_API int mxw_accumulate_block_gram(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ld,
+                              float* gram_blocks, void* stream);
+
+/*
+ * One pass over x computing any subset of sum_abs / sum_sq (as
+ * mxw_accumulate_moments) and gram_blocks (as mxw_accumulate_block_gram);
+ * NULL outputs are skipped.  ActivationCollector.update with several
+ * objectives (mxwave/calibration.py:226-236) reads its input once this way.
+ * flags: device uint32 word for MXW_FLAG_TIMEOUT, or NULL.
+ */
+MXW_API int mxw_accumulate_activation_stats(const void* x, int dtype, int64_t tokens, int64_t cols,
+                                    int64_t ld, float* sum_abs, float* sum_sq,
+                                    float* gram_blocks, uint32_t* flags, void* stream);
+
+/*
+ * mean_abs = sum_abs / count, rms = sqrt(sum_sq / count) (either output may be
+ * NULL).  Replaces ActivationCollector.finalize for the moment objectives
+ * (mxwave/calibration.py:262-266).
+ */
+MXW_API int mxw_finalize_moments(const float* sum_abs, const float* sum_sq, int64_t cols, int64_t count,
+                         float* mean_abs, float* rms, void* stream);
+
+/*
+ * Block Hessian = G / count with diagonal damping (absolute: + damp; relative:
+ * + damp * mean(block diagonal)).  `full` = 0: G is gram_blocks
+ * [cols/32,32,32]; `full` = 1: G is a full [cols, cols] Gram with row stride
+ * ldg whose diagonal 32x32 blocks are taken.  out: [cols/32, 32, 32].
+ * Replaces ActivationCollector.finalize for "block-hessian"
+ * (mxwave/calibration.py:267-270) and _damp_block_hessian (core.py:61-69).
+ */
+MXW_API int mxw_finalize_block_hessian(const float* gram, int full, int64_t cols, int64_t ldg,
+                               int64_t count, double damp, int mode, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXWAVE_B200_H_ */

@@ -1,0 +1,121 @@
+"""GPU parity of the calibration statistics kernels (through the C ABI)
+against the float64 oracle.  Bar: 1e-5 relative (fp32 accumulation)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from mxwave_b200 import _lib
+from mxwave_b200 import synthetic as syn
+from mxwave_b200.core import compute_block_hessian
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+
+
+def _stream(dev) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _gram_err(got: np.ndarray, ref: np.ndarray) -> float:
+    """max |dG_ij| / sqrt(G_ii G_jj) over each 32x32 block (Cauchy-Schwarz scale)."""
+    d = np.einsum("bii->bi", ref)
+    scale = np.sqrt(np.maximum(d[:, :, None] * d[:, None, :], 1e-300))
+    return float(np.max(np.abs(got - ref) / scale))
+
+
+def _x(tokens: int, cols: int, seed: int, dev, dtype=torch.bfloat16):
+    bits = syn.det_activations(tokens, cols, seed)
+    xf = syn.bf16_bits_to_f32(bits)
+    t = torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).to(dev)
+    if dtype != torch.bfloat16:
+        t = t.to(dtype)
+        xf = t.float().cpu().numpy()
+    return t, xf.astype(np.float64)
+
+
+SIZES = [(1, 32), (7, 64), (300, 96), (1000, 160), (8192, 5120), (4097, 544)]
+
+
+@pytest.mark.parametrize("tokens,cols", SIZES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_moments_and_block_gram(tokens, cols, dtype, cuda_device) -> None:
+    if dtype != torch.bfloat16 and tokens > 5000:
+        pytest.skip("large case covered in bf16")
+    lib = _lib.load()
+    x, xf = _x(tokens, cols, tokens + cols, cuda_device, dtype)
+    s1 = torch.zeros(cols, device=cuda_device)
+    s2 = torch.zeros(cols, device=cuda_device)
+    g = torch.zeros(cols // 32, 32, 32, device=cuda_device)
+    code = {torch.bfloat16: _lib.MXW_BF16, torch.float16: _lib.MXW_F16, torch.float32: _lib.MXW_F32}[dtype]
+    st = lib.mxw_accumulate_activation_stats(x.data_ptr(), code, tokens, cols, cols, s1.data_ptr(),
+                                             s2.data_ptr(), g.data_ptr(), None, _stream(cuda_device))
+    assert st == _lib.MXW_OK
+    torch.cuda.synchronize()
+    r1, r2 = oracle.moments(xf)
+    np.testing.assert_allclose(s1.cpu().numpy(), r1, rtol=RTOL)
+    np.testing.assert_allclose(s2.cpu().numpy(), r2, rtol=RTOL)
+    assert _gram_err(g.cpu().numpy(), oracle.block_gram(xf)) < RTOL
+
+
+def test_accumulation_across_calls_and_ragged_width(cuda_device) -> None:
+    lib = _lib.load()
+    x, xf = _x(3000, 5120, 5, cuda_device)
+    s2 = torch.zeros(5120, device=cuda_device)
+    g = torch.zeros(160, 32, 32, device=cuda_device)
+    for a, b in ((0, 1000), (1000, 1001), (1001, 3000)):
+        part = x[a:b]
+        assert lib.mxw_accumulate_activation_stats(part.data_ptr(), _lib.MXW_BF16, b - a, 5120, 5120, None,
+                                                   s2.data_ptr(), g.data_ptr(), None, _stream(cuda_device)) == 0
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(s2.cpu().numpy(), oracle.moments(xf)[1], rtol=RTOL)
+    assert _gram_err(g.cpu().numpy(), oracle.block_gram(xf)) < RTOL
+    # Width not divisible by 32 (moments only) and a strided view (plain path).
+    y, yf = _x(500, 70, 6, cuda_device)
+    s1 = torch.zeros(70, device=cuda_device)
+    assert lib.mxw_accumulate_moments(y.data_ptr(), _lib.MXW_BF16, 500, 70, 70, s1.data_ptr(), None,
+                                      _stream(cuda_device)) == 0
+    z = x[:, 1:1025]
+    sz = torch.zeros(1024, device=cuda_device)
+    assert lib.mxw_accumulate_moments(z.data_ptr(), _lib.MXW_BF16, 3000, 1024, z.stride(0), None, sz.data_ptr(),
+                                      _stream(cuda_device)) == 0
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(s1.cpu().numpy(), oracle.moments(yf)[0], rtol=RTOL)
+    np.testing.assert_allclose(sz.cpu().numpy(), oracle.moments(xf[:, 1:1025])[1], rtol=RTOL)
+
+
+@pytest.mark.parametrize("mode", ["absolute", "relative"])
+def test_compute_block_hessian_matches_oracle(mode, cuda_device) -> None:
+    x, xf = _x(2048, 1024, 9, cuda_device)
+    h = compute_block_hessian(x, damp=1e-3, damp_mode=mode).cpu().numpy()
+    ref = oracle.finalize_block_hessian(oracle.block_gram(xf), 2048, 1e-3, mode)
+    assert _gram_err(h, ref) < RTOL
+
+
+def test_finalize_moments(cuda_device) -> None:
+    lib = _lib.load()
+    s1 = torch.rand(333, device=cuda_device) * 100
+    s2 = torch.rand(333, device=cuda_device) * 100
+    ma = torch.empty(333, device=cuda_device)
+    rms = torch.empty(333, device=cuda_device)
+    assert lib.mxw_finalize_moments(s1.data_ptr(), s2.data_ptr(), 333, 77, ma.data_ptr(), rms.data_ptr(),
+                                    _stream(cuda_device)) == 0
+    torch.cuda.synchronize()
+    # Same fp32 operations as the reference's finalize (calibration.py:262-266).
+    assert torch.equal(ma, s1 / 77)
+    assert torch.equal(rms, torch.sqrt(s2 / 77))
+
+
+def test_dequant_matches_oracle(cuda_device) -> None:
+    from mxwave_b200.core import dequant_mxfp4, quantize_mxfp4
+
+    w = syn.det_dense_weight(33, 256, 4, outlier_fraction=0.05)
+    wt = torch.from_numpy(w.view(np.int16).copy()).view(torch.bfloat16).to(cuda_device)
+    p, s = quantize_mxfp4(wt)
+    d = dequant_mxfp4(p, s, (33, 256)).cpu().numpy()
+    ref = oracle.dequant_mxfp4(p.cpu().numpy(), s.cpu().numpy(), 256)
+    np.testing.assert_array_equal(d, ref)
