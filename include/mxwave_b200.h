@@ -118,6 +118,17 @@ MXW_API int mxw_accumulate_activation_stats(const void* x, int dtype, int64_t to
                                     float* gram_blocks, uint32_t* flags, void* stream);
 
 /*
+ * Full X^T X of bf16 activations x [tokens, cols] (row stride ld elements),
+ * fp32 accumulation on the tcgen05 tensor cores, added into gram [cols, cols]
+ * (row stride ldg).  The reference forms only the diagonal 32x32 blocks
+ * (mxwave/calibration.py:233-236, core.py:55-56); the full product is the
+ * calibration workload of the Hessian objective.  Requires cols % 128 == 0,
+ * ld % 8 == 0, 16-byte aligned x and gram.  flags: MXW_FLAG_TIMEOUT or NULL.
+ */
+MXW_API int mxw_accumulate_xtx(const void* x, int64_t tokens, int64_t cols, int64_t ld, float* gram,
+                               int64_t ldg, uint32_t* flags, void* stream);
+
+/*
  * mean_abs = sum_abs / count, rms = sqrt(sum_sq / count) (either output may be
  * NULL).  Replaces ActivationCollector.finalize for the moment objectives
  * (mxwave/calibration.py:262-266).

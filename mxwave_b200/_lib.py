@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mxw_accumulate_moments": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _vp]),
     "mxw_accumulate_block_gram": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp]),
     "mxw_accumulate_activation_stats": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "mxw_accumulate_xtx": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "mxw_finalize_moments": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _vp]),
     "mxw_finalize_block_hessian": (_int, [_vp, _int, _i64, _i64, _i64, ctypes.c_double, _int, _vp, _vp]),
 }

@@ -78,26 +78,47 @@ __device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigne
   return d;
 }
 
+// Correctly rounded packed product for a result that feeds an addition.
+// ptxas contracts "mul.rn.f32x2 -> add.rn.f32x2" into a single fma even with
+// the explicit rounding modifier (measured on sm_100a), which would skip the
+// product's rounding.  An fma with a -0 addend rounds exactly like the
+// multiply (a*b + -0 == a*b, signed zeros included) and leaves nothing to
+// contract.  `nz2` must be -0.0 in both halves and come from a runtime value
+// (a kernel argument), so the compiler cannot rewrite the fma as a multiply.
+__device__ __forceinline__ unsigned long long mul2_rounded(unsigned long long a, unsigned long long b,
+                                                           unsigned long long nz2) {
+  return fma2(a, b, nz2);
+}
+
 // ----------------------------------------------------------------- E2M1 codes
 
 // Two fp32 values -> one byte of E2M1 codes, `lo` in bits 0-3 and `hi` in bits
 // 4-7, rounded to nearest with ties to even and saturated to +-6 (the
 // reference's clamp(-6, 6) followed by its tie-to-even bucket rule).
 __device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
-  uint16_t r;
-  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}"
-      : "=h"(r)
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}"
+      : "=r"(r)
       : "f"(hi), "f"(lo));
   return r;
 }
 
-// One byte of two E2M1 codes -> the two magnitudes*sign as fp32 (exact).
-__device__ __forceinline__ unsigned long long e2m1x2_to_f32x2(uint32_t byte) {
-  uint32_t h2;
-  uint16_t b16 = static_cast<uint16_t>(byte);
-  asm("{\n\t.reg .b8 t;\n\tcvt.u8.u16 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "h"(b16));
-  __half2 hh = *reinterpret_cast<__half2*>(&h2);
+// Two non-negative E2M1 codes (0..7, one per nibble of `byte`) -> their
+// magnitudes as an fp32 pair, through two byte permutes: the f16 encodings of
+// {0, 0.5, 1, 1.5, 2, 3, 4, 6} differ only in their high byte, so a byte
+// table lookup yields an exact f16x2 that converts to fp32 exactly.
+__device__ __forceinline__ unsigned long long e2m1_mag_to_f32x2(uint32_t byte) {
+  const uint32_t u = __byte_perm(0x3E3C3800u, 0x46444240u, byte);  // [HB[c0], HB[c1], 0, 0]
+  uint32_t h = __byte_perm(u, 0u, 0x1404u);                         // [0, HB[c0], 0, HB[c1]]
+  const __half2 hh = *reinterpret_cast<__half2*>(&h);
   return pack2(__low2float(hh), __high2float(hh));
+}
+
+// Signed E2M1 codes (one per nibble) -> signed fp32 magnitudes (dequantisation).
+__device__ __forceinline__ unsigned long long e2m1x2_to_f32x2(uint32_t byte) {
+  const unsigned long long m = e2m1_mag_to_f32x2(byte & 0x77u);
+  const uint32_t s0 = (byte & 0x08u) << 28, s1 = (byte & 0x80u) << 24;
+  return m ^ ((static_cast<unsigned long long>(s1) << 32) | s0);
 }
 
 }  // namespace mxw

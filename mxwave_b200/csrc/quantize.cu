@@ -8,19 +8,28 @@
 //     p[0] + p[1] + ... + p[7] left to right (mean then divides by 32);
 //   * einsum("obs,bsd->obd", dW, H) (core.py:228): per output d the fp32 FMA
 //     chain over s = 0..31.
+// The unweighted and gamma errors only need dW^2, so they are evaluated on
+// magnitudes: |dW| = q(|t|/2^e) * 2^e - |t|.  Per element pair and candidate:
+// one packed multiply, one E2M1 conversion (XU pipe), two byte permutes that
+// decode the codes to an exact f16x2, and packed fp32 FMA / multiply / add.
+//
 // Data layout: one thread owns one 32-element block.  A warp owns one block
 // column and 32 consecutive rows, so gamma and the block's 32x32 Hessian are
-// shared by the whole warp (register / shared-memory broadcast).
+// shared by the whole warp (registers / shared-memory broadcast).
 //
-// Pipeline: persistent CTAs, one TMA producer warp + 8 consumer warps.  A tile
-// is 32 rows x 256 columns (8 block columns), loaded by TMA with the 128-byte
-// swizzle into a ring of shared-memory stages; with the swizzle, the 8 lanes
-// of a shared-memory phase (8 consecutive rows, same chunk) hit 8 distinct
-// bank groups.
+// Pipeline: persistent CTAs (one wave: #SMs x occupancy), each owning a
+// contiguous range of tiles in strip-major order; one TMA producer warp + 8
+// consumer warps.  A tile is 32 rows x 256 columns (8 block columns) loaded by
+// TMA with the 128-byte swizzle into a ring of shared-memory stages; with the
+// swizzle, the 8 lanes of a shared-memory phase (8 consecutive rows, same
+// chunk) hit 8 distinct bank groups.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "runtime.h"
@@ -39,7 +48,7 @@ enum Obj { kObjNone = 0, kObjGamma = 1, kObjHess = 2, kObjRtn = 3 };
 enum QMode { kQAmax = 0, kQTop2 = 1, kQGeneral = 2 };
 
 struct QuantParams {
-  int64_t rows, cols, nb, n_row_tiles;
+  int64_t rows, cols, nb, n_row_tiles, n_tiles;
   const float* gamma;
   const float* hessian;
   uint8_t* packed;
@@ -48,104 +57,145 @@ struct QuantParams {
   int depth;
   int q_below, q_above, q_small;
   float q_w;
+  // Always 0.0f.  Added to the scaled values before encoding so that -0
+  // becomes +0 (code 0, as the reference's "scaled < 0" sign rule gives); a
+  // runtime operand keeps the compiler from folding "x + 0" into "x".
+  float zero;
+  // Always -0.0f: the addend of mul2_rounded (see common.cuh).
+  float negzero;
 };
 
 template <int DT>
-struct Elem;
-template <>
-struct Elem<MXW_BF16> {
-  static constexpr int kBytes = 2;
+struct Elem {
+  static constexpr int kBytes = DT == MXW_F32 ? 4 : 2;
+  static constexpr int kBoxCols = 128 / kBytes;
+  static constexpr int kBoxesPerStage = kTileBlocks * kBlock * kBytes / 128;
+  static constexpr int kStageBytes = kBoxesPerStage * kBoxBytes;
 };
-template <>
-struct Elem<MXW_F16> {
-  static constexpr int kBytes = 2;
+
+// Everything a thread knows about its block after loading it.  2-byte inputs
+// keep their raw words (16 registers); fp32 inputs keep the signed pairs.
+// Both keep nt2 = -|t| as fp32 pairs (elements 2j, 2j+1), the input of the
+// error evaluation.
+template <int DT>
+struct BlockData {
+  static constexpr bool kWords = DT != MXW_F32;
+  uint32_t words[kWords ? 16 : 1];
+  unsigned long long t2[kWords ? 1 : 16];
+  unsigned long long nt2[16];
+  float amax, second;  // largest / second-largest magnitude
+  bool nonfinite;
+
+  // Signed element pair j as fp32.
+  __device__ __forceinline__ unsigned long long signed_pair(int j) const {
+    if constexpr (DT == MXW_BF16) {
+      return pack2(bits_f32(words[j] << 16), bits_f32(words[j] & 0xffff0000u));
+    } else if constexpr (DT == MXW_F16) {
+      const __half2 h = *reinterpret_cast<const __half2*>(&words[j]);
+      return pack2(__low2float(h), __high2float(h));
+    } else {
+      return t2[j];
+    }
+  }
+  // Sign bits of element pair j, positioned as fp32 sign bits of a pair.
+  __device__ __forceinline__ unsigned long long sign_pair(int j) const {
+    if constexpr (kWords) {
+      return (static_cast<unsigned long long>(words[j] & 0x80000000u) << 32) |
+             static_cast<unsigned long long>((words[j] & 0x8000u) << 16);
+    } else {
+      return t2[j] & 0x8000000080000000ull;
+    }
+  }
 };
-template <>
-struct Elem<MXW_F32> {
-  static constexpr int kBytes = 4;
-};
+
+__device__ __forceinline__ unsigned long long neg_abs2(unsigned long long v) {
+  return v | 0x8000000080000000ull;
+}
 
 // ------------------------------------------------------------ block loading
 
-// Read this thread's block (row `lane` of the tile, block column `w`) from a
-// swizzled stage.  Produces 16 fp32 pairs (elements 2j, 2j+1), the block's
-// largest and second-largest magnitude, and whether it holds a NaN/inf.
 template <int DT, int QM>
-__device__ __forceinline__ void read_block_smem(const uint8_t* stage, int w, int lane,
-                                                unsigned long long (&t2)[16], float& amax,
-                                                float& second, bool& nonfinite) {
+__device__ __forceinline__ void finish_stats_16bit(BlockData<DT>& B) {
+  // Magnitude order statistics on the raw 16-bit patterns (sign-magnitude:
+  // the integer order of |bits| is the order of |value|; NaN/inf on top).
+  uint32_t m1 = 0, m2 = 0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const uint32_t a = B.words[k] & 0x7fff7fffu;
+    if constexpr (QM == kQTop2) m2 = __vmaxu2(m2, __vminu2(m1, a));
+    m1 = __vmaxu2(m1, a);
+  }
+  const uint32_t lo1 = m1 & 0xffffu, hi1 = m1 >> 16;
+  const uint32_t top1 = max(lo1, hi1);
+  uint32_t top2 = 0;
+  if constexpr (QM == kQTop2) top2 = max(min(lo1, hi1), max(m2 & 0xffffu, m2 >> 16));
+  if constexpr (DT == MXW_BF16) {
+    B.nonfinite = top1 >= 0x7f80u;
+    B.amax = bits_f32(top1 << 16);
+    B.second = bits_f32(top2 << 16);
+  } else {
+    B.nonfinite = top1 >= 0x7c00u;
+    B.amax = __half2float(__ushort_as_half(static_cast<unsigned short>(top1)));
+    B.second = __half2float(__ushort_as_half(static_cast<unsigned short>(top2)));
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) B.nt2[k] = neg_abs2(B.signed_pair(k));
+}
+
+template <int DT, int QM>
+__device__ __forceinline__ void finish_stats_f32(BlockData<DT>& B, const unsigned long long (&t2)[16]) {
+  uint32_t m1 = 0, m2 = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const f2 v = unpack2(t2[j]);
+    const uint32_t a0 = f32_bits(v.x) & 0x7fffffffu, a1 = f32_bits(v.y) & 0x7fffffffu;
+    if constexpr (QM == kQTop2) m2 = max(m2, min(m1, a0));
+    m1 = max(m1, a0);
+    if constexpr (QM == kQTop2) m2 = max(m2, min(m1, a1));
+    m1 = max(m1, a1);
+    B.nt2[j] = neg_abs2(t2[j]);
+  }
+  B.nonfinite = m1 >= 0x7f800000u;
+  B.amax = bits_f32(m1);
+  B.second = bits_f32(m2);
+}
+
+// Read this thread's block (row `lane` of the tile, block column `w`) from a
+// swizzled stage.
+template <int DT, int QM>
+__device__ __forceinline__ void read_block_smem(const uint8_t* stage, int w, int lane, BlockData<DT>& B) {
   if constexpr (Elem<DT>::kBytes == 2) {
     const uint8_t* box = stage + (w >> 1) * kBoxBytes + lane * 128;
-    uint32_t words[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int c = (4 * (w & 1) + j) ^ (lane & 7);
-      uint4 v = *reinterpret_cast<const uint4*>(box + (c << 4));
-      words[4 * j + 0] = v.x;
-      words[4 * j + 1] = v.y;
-      words[4 * j + 2] = v.z;
-      words[4 * j + 3] = v.w;
+      const uint4 v = *reinterpret_cast<const uint4*>(box + (c << 4));
+      B.words[4 * j + 0] = v.x;
+      B.words[4 * j + 1] = v.y;
+      B.words[4 * j + 2] = v.z;
+      B.words[4 * j + 3] = v.w;
     }
-    // Magnitude order statistics on the raw 16-bit patterns (sign-magnitude:
-    // the integer order of |bits| is the order of |value|; NaN/inf on top).
-    uint32_t m1 = 0, m2 = 0;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const uint32_t a = words[k] & 0x7fff7fffu;
-      if constexpr (QM == kQTop2) m2 = __vmaxu2(m2, __vminu2(m1, a));
-      m1 = __vmaxu2(m1, a);
-    }
-    const uint32_t lo1 = m1 & 0xffffu, hi1 = m1 >> 16;
-    const uint32_t top1 = max(lo1, hi1);
-    uint32_t top2 = 0;
-    if constexpr (QM == kQTop2) top2 = max(min(lo1, hi1), max(m2 & 0xffffu, m2 >> 16));
-    if constexpr (DT == MXW_BF16) {
-      nonfinite = top1 >= 0x7f80u;
-      amax = bits_f32(top1 << 16);
-      second = bits_f32(top2 << 16);
-#pragma unroll
-      for (int k = 0; k < 16; ++k) t2[k] = pack2(bits_f32(words[k] << 16), bits_f32(words[k] & 0xffff0000u));
-    } else {
-      nonfinite = top1 >= 0x7c00u;
-      amax = __half2float(__ushort_as_half(static_cast<unsigned short>(top1)));
-      second = __half2float(__ushort_as_half(static_cast<unsigned short>(top2)));
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        __half2 h = *reinterpret_cast<__half2*>(&words[k]);
-        t2[k] = pack2(__low2float(h), __high2float(h));
-      }
-    }
+    finish_stats_16bit<DT, QM>(B);
   } else {
     const uint8_t* box = stage + w * kBoxBytes + lane * 128;
-    uint32_t m1 = 0, m2 = 0;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const int cs = c ^ (lane & 7);
-      float4 v = *reinterpret_cast<const float4*>(box + (cs << 4));
-      t2[2 * c] = pack2(v.x, v.y);
-      t2[2 * c + 1] = pack2(v.z, v.w);
-      const uint32_t a[4] = {f32_bits(v.x) & 0x7fffffffu, f32_bits(v.y) & 0x7fffffffu,
-                             f32_bits(v.z) & 0x7fffffffu, f32_bits(v.w) & 0x7fffffffu};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if constexpr (QM == kQTop2) m2 = max(m2, min(m1, a[k]));
-        m1 = max(m1, a[k]);
-      }
+      const float4 v = *reinterpret_cast<const float4*>(box + ((c ^ (lane & 7)) << 4));
+      B.t2[2 * c] = pack2(v.x, v.y);
+      B.t2[2 * c + 1] = pack2(v.z, v.w);
     }
-    nonfinite = m1 >= 0x7f800000u;
-    amax = bits_f32(m1);
-    second = bits_f32(m2);
+    finish_stats_f32<DT, QM>(B, B.t2);
   }
 }
 
 // k-th smallest magnitude (0-based) of the block, by rank counting.
-__device__ __forceinline__ float kth_magnitude(const unsigned long long (&t2)[16], int k) {
+__device__ __forceinline__ float kth_magnitude(const unsigned long long (&nt2)[16], int k) {
   float a[32];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    f2 v = unpack2(t2[j]);
-    a[2 * j] = fabsf(v.x);
-    a[2 * j + 1] = fabsf(v.y);
+    const f2 v = unpack2(nt2[j]);
+    a[2 * j] = -v.x;
+    a[2 * j + 1] = -v.y;
   }
   float result = 0.0f;
 #pragma unroll
@@ -163,15 +213,23 @@ __device__ __forceinline__ float kth_magnitude(const unsigned long long (&t2)[16
 
 // ------------------------------------------------------------- error kernels
 
-// Error of one candidate exponent e for the unweighted / gamma objectives:
-// mean over the block of dW^2 (times gamma^2), dW = RNE(clamp(t/2^e)) * 2^e - t
-// (core.py:224-234).  Computed as -dW = q' * 2^e + t with q' = RNE(t * -2^-e):
-// the product is exact, so the fused form rounds like the reference's
+// |dW| for one element pair: q(|t| / 2^e) * 2^e - |t|, with nt = -|t|.  The
+// product q*2^e is exact, so the fused form rounds like the reference's
 // separate multiply and subtract, except when q*2^e overflows (e >= 126),
 // which takes the unfused path.
+__device__ __forceinline__ unsigned long long abs_dw2(unsigned long long nt, unsigned long long NI2,
+                                                      unsigned long long S2, bool unfused,
+                                                      unsigned long long NZ2) {
+  const f2 x = unpack2(mul2(nt, NI2));  // |t| / 2^e exactly (NI2 = -2^-e)
+  const unsigned long long q = e2m1_mag_to_f32x2(e2m1x2(x.x, x.y));
+  return unfused ? add2(mul2_rounded(q, S2, NZ2), nt) : fma2(q, S2, nt);
+}
+
+// Unweighted / gamma error of one candidate exponent e: mean over the block of
+// dW^2 (times gamma^2), core.py:224-234.
 template <bool GAMMA>
-__device__ __forceinline__ float candidate_error(const unsigned long long (&t2)[16], int e,
-                                                 const unsigned long long (&g2)[16]) {
+__device__ __forceinline__ float candidate_error(const unsigned long long (&nt2)[16], int e,
+                                                 const unsigned long long (&g2)[16], unsigned long long NZ2) {
   const float s = exp2i(e);
   const float ninv = -exp2i(-e);
   const unsigned long long S2 = pack2(s, s), NI2 = pack2(ninv, ninv);
@@ -182,11 +240,10 @@ __device__ __forceinline__ float candidate_error(const unsigned long long (&t2)[
 #pragma unroll
     for (int lp = 0; lp < 4; ++lp) {
       const int j = q * 4 + lp;
-      const f2 y = unpack2(mul2(t2[j], NI2));
-      const unsigned long long qv = e2m1x2_to_f32x2(e2m1x2(y.x, y.y));
-      const unsigned long long d = unfused ? add2(mul2(qv, S2), t2[j]) : fma2(qv, S2, t2[j]);
-      unsigned long long sq = mul2(d, d);
-      if constexpr (GAMMA) sq = mul2(sq, g2[j]);
+      const unsigned long long d = abs_dw2(nt2[j], NI2, S2, unfused, NZ2);
+      // fl(dW^2), then fl(fl(dW^2) * gamma^2): each product rounded before the add.
+      unsigned long long sq = mul2_rounded(d, d, NZ2);
+      if constexpr (GAMMA) sq = mul2_rounded(sq, g2[j], NZ2);
       p[lp] = (q == 0) ? sq : add2(p[lp], sq);
     }
   }
@@ -203,36 +260,48 @@ __device__ __forceinline__ float candidate_error(const unsigned long long (&t2)[
 
 // Block-Hessian error of one candidate: sum_d (sum_s dW_s H[s,d]) dW_d with
 // the inner sum as a sequential fp32 FMA chain over s (core.py:228-229).
-// Evaluated on -dW: every product flips sign twice, so the result is equal.
-__device__ __forceinline__ float candidate_error_hessian(const unsigned long long (&t2)[16], int e,
-                                                         const float* __restrict__ Hs) {
+// dW = sign(t) * |dW| (sign bit transferred exactly); dW pairs are rebuilt on
+// the fly instead of being held in 32 registers.
+// One 16-byte row fragment of the block Hessian.  Volatile loads: H is the
+// same for every candidate, and letting the compiler hoist all 256 fragments
+// out of the candidate loop would spill them to local memory.
+template <bool SHARED>
+__device__ __forceinline__ ulonglong2 load_h16(const float* p) {
+  ulonglong2 v;
+  if constexpr (SHARED) {
+    asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "r"(smem_u32(p)));
+  } else {
+    asm volatile("ld.global.nc.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p));
+  }
+  return v;
+}
+
+template <int DT, bool HS_SHARED>
+__device__ __forceinline__ float candidate_error_hessian(const BlockData<DT>& B, int e, const float* Hs,
+                                                         unsigned long long NZ2) {
   const float s = exp2i(e);
   const float ninv = -exp2i(-e);
   const unsigned long long S2 = pack2(s, s), NI2 = pack2(ninv, ninv);
   const bool unfused = e >= 126;
-  float nd[32];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const f2 y = unpack2(mul2(t2[j], NI2));
-    const unsigned long long qv = e2m1x2_to_f32x2(e2m1x2(y.x, y.y));
-    const f2 d = unpack2(unfused ? add2(mul2(qv, S2), t2[j]) : fma2(qv, S2, t2[j]));
-    nd[2 * j] = d.x;
-    nd[2 * j + 1] = d.y;
-  }
   unsigned long long w[16];
 #pragma unroll
-  for (int si = 0; si < 32; ++si) {
-    const unsigned long long ds = pack2(nd[si], nd[si]);
-    const ulonglong2* row = reinterpret_cast<const ulonglong2*>(Hs + si * 32);
+  for (int sp = 0; sp < 16; ++sp) {
+    const f2 d = unpack2(abs_dw2(B.nt2[sp], NI2, S2, unfused, NZ2) ^ B.sign_pair(sp));
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const ulonglong2 h = row[k];
-      if (si == 0) {
-        w[2 * k] = mul2(ds, h.x);
-        w[2 * k + 1] = mul2(ds, h.y);
-      } else {
-        w[2 * k] = fma2(ds, h.x, w[2 * k]);
-        w[2 * k + 1] = fma2(ds, h.y, w[2 * k + 1]);
+    for (int h = 0; h < 2; ++h) {
+      const int si = 2 * sp + h;
+      const float dv = h ? d.y : d.x;
+      const unsigned long long ds = pack2(dv, dv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const ulonglong2 hv = load_h16<HS_SHARED>(Hs + si * 32 + 4 * k);
+        if (si == 0) {
+          w[2 * k] = mul2(ds, hv.x);
+          w[2 * k + 1] = mul2(ds, hv.y);
+        } else {
+          w[2 * k] = fma2(ds, hv.x, w[2 * k]);
+          w[2 * k + 1] = fma2(ds, hv.y, w[2 * k + 1]);
+        }
       }
     }
   }
@@ -242,7 +311,8 @@ __device__ __forceinline__ float candidate_error_hessian(const unsigned long lon
 #pragma unroll
     for (int lp = 0; lp < 4; ++lp) {
       const int j = q * 4 + lp;
-      const unsigned long long prod = mul2(w[j], pack2(nd[2 * j], nd[2 * j + 1]));
+      const unsigned long long d = abs_dw2(B.nt2[j], NI2, S2, unfused, NZ2) ^ B.sign_pair(j);
+      const unsigned long long prod = mul2_rounded(w[j], d, NZ2);
       p[lp] = (q == 0) ? prod : add2(p[lp], prod);
     }
   }
@@ -268,98 +338,112 @@ __device__ __forceinline__ int rtn_exponent(float block_max) {
 
 // ------------------------------------------------------------- block driver
 
-// Chooses the exponent and encodes one block.  Returns the E8M0 byte and
-// writes 16 packed bytes.
-template <int OBJ, int QM>
-__device__ __forceinline__ uint32_t quantize_one_block(unsigned long long (&t2)[16], float amax,
-                                                       float second, const QuantParams& P,
-                                                       const unsigned long long (&g2)[16],
-                                                       const float* Hs, uint4& packed) {
+// Chooses the exponent and encodes one block into 16 packed bytes; returns the
+// E8M0 byte.  `Hs`: the block's Hessian (shared or global memory) or unused.
+template <int DT, int OBJ, int QM, bool HS_SHARED>
+__device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, const QuantParams& P,
+                                                       const unsigned long long (&g2)[16], const float* Hs,
+                                                       uint4& packed) {
   int raw;
   if constexpr (OBJ == kObjRtn) {
-    raw = rtn_exponent(amax);
+    // core.py:240-243: the exponent is clamped to [-127, 127] before storage.
+    raw = max(-127, min(127, rtn_exponent(B.amax)));
   } else {
     float anchor;
     if constexpr (QM == kQAmax) {
-      anchor = amax;
+      anchor = B.amax;
     } else {
       float lo, hi;
       if constexpr (QM == kQTop2) {
-        lo = P.q_below == 31 ? amax : second;
-        hi = P.q_above == 31 ? amax : second;
+        lo = P.q_below == 31 ? B.amax : B.second;
+        hi = P.q_above == 31 ? B.amax : B.second;
       } else {
-        lo = kth_magnitude(t2, P.q_below);
-        hi = (P.q_above == P.q_below) ? lo : kth_magnitude(t2, P.q_above);
+        lo = kth_magnitude(B.nt2, P.q_below);
+        hi = (P.q_above == P.q_below) ? lo : kth_magnitude(B.nt2, P.q_above);
       }
       const float d = __fsub_rn(hi, lo);
       anchor = P.q_small ? __fmaf_rn(P.q_w, d, lo) : __fmaf_rn(__fsub_rn(P.q_w, 1.0f), d, hi);
     }
-    const bool near_zero = amax < 1e-6f;
+    const bool near_zero = B.amax < 1e-6f;
     anchor = fmaxf(anchor, 1e-6f);
     const int floor_e = floor_log2_f32(__fdiv_rn(anchor, 6.0f));
     const int lo_e = max(-127, min(127, floor_e - P.depth));
     if (near_zero) {
-      // t is replaced by zeros (core.py:194-195): every candidate has error 0
-      // and the first candidate wins the strict-< argmin.
-#pragma unroll
-      for (int j = 0; j < 16; ++j) t2[j] = 0ull;
-      raw = lo_e;
-    } else {
-      const int hi_e = max(-127, min(127, floor_e + 1));
-      const int safe_e = max(-127, min(127, ceil_log2_f32(__fdiv_rn(fmaxf(amax, 1e-12f), 6.0f))));
-      float best = __int_as_float(0x7f800000);
-      raw = lo_e;
-      int prev = -1000;
-      // Candidates floor-depth .. floor+1 (clamped: equal neighbours are
-      // skipped, their error would be identical and never strictly smaller),
-      // then the no-clipping exponent unless it repeats one of them.
-      for (int k = 0; k <= P.depth + 2; ++k) {
-        int e;
-        if (k <= P.depth + 1) {
-          e = max(-127, min(127, floor_e - P.depth + k));
-          if (e == prev) continue;
-          prev = e;
-        } else {
-          e = safe_e;
-          if (e >= lo_e && e <= hi_e) continue;
-        }
-        float err;
-        if constexpr (OBJ == kObjHess) {
-          err = candidate_error_hessian(t2, e, Hs);
-        } else {
-          err = candidate_error<OBJ == kObjGamma>(t2, e, g2);
-        }
-        if (err < best) raw = e;
-        best = (isnan(err) || isnan(best)) ? __int_as_float(0x7fffffff) : fminf(best, err);
+      // t is replaced by zeros (core.py:194-195): every candidate has error 0,
+      // the first candidate wins the strict-< argmin and every code is 0.
+      packed = make_uint4(0u, 0u, 0u, 0u);
+      return static_cast<uint32_t>(lo_e + 127);
+    }
+    const int hi_e = max(-127, min(127, floor_e + 1));
+    const int safe_e = max(-127, min(127, ceil_log2_f32(__fdiv_rn(fmaxf(B.amax, 1e-12f), 6.0f))));
+    const unsigned long long NZ2 = pack2(P.negzero, P.negzero);
+    float best = __int_as_float(0x7f800000);
+    raw = lo_e;
+    // Candidates floor-depth .. floor+1 (clamped: equal neighbours are skipped,
+    // their error would be identical and never strictly smaller), then the
+    // no-clipping exponent unless it repeats one of them.
+    const int n_seq = hi_e - lo_e + 1;
+    const bool safe_new = safe_e < lo_e || safe_e > hi_e;
+    for (int k = 0; k < n_seq + (safe_new ? 1 : 0); ++k) {
+      const int e = k < n_seq ? lo_e + k : safe_e;
+      float err;
+      if constexpr (OBJ == kObjHess) {
+        err = candidate_error_hessian<DT, HS_SHARED>(B, e, Hs, NZ2);
+      } else {
+        err = candidate_error<OBJ == kObjGamma>(B.nt2, e, g2, NZ2);
       }
+      if (err < best) raw = e;
+      best = (isnan(err) || isnan(best)) ? __int_as_float(0x7fffffff) : fminf(best, err);
     }
   }
   // Final encode (core.py:242-249): x = clamp(t / 2^raw) -> nibble, -0 -> code 0.
   const float inv = exp2i(-raw);
   const unsigned long long I2 = pack2(inv, inv);
-  const unsigned long long Z2 = 0ull;
+  const unsigned long long Z2 = pack2(P.zero, P.zero);
+  const unsigned long long NZ2e = pack2(P.negzero, P.negzero);
   uint32_t bytes[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    const f2 x = unpack2(add2(mul2(t2[j], I2), Z2));
+    const f2 x = unpack2(add2(mul2_rounded(B.signed_pair(j), I2, NZ2e), Z2));
     bytes[j] = e2m1x2(x.x, x.y);
   }
-  packed.x = bytes[0] | (bytes[1] << 8) | (bytes[2] << 16) | (bytes[3] << 24);
-  packed.y = bytes[4] | (bytes[5] << 8) | (bytes[6] << 16) | (bytes[7] << 24);
-  packed.z = bytes[8] | (bytes[9] << 8) | (bytes[10] << 16) | (bytes[11] << 24);
-  packed.w = bytes[12] | (bytes[13] << 8) | (bytes[14] << 16) | (bytes[15] << 24);
+  packed.x = __byte_perm(__byte_perm(bytes[0], bytes[1], 0x0040), __byte_perm(bytes[2], bytes[3], 0x0040), 0x5410);
+  packed.y = __byte_perm(__byte_perm(bytes[4], bytes[5], 0x0040), __byte_perm(bytes[6], bytes[7], 0x0040), 0x5410);
+  packed.z = __byte_perm(__byte_perm(bytes[8], bytes[9], 0x0040), __byte_perm(bytes[10], bytes[11], 0x0040), 0x5410);
+  packed.w =
+      __byte_perm(__byte_perm(bytes[12], bytes[13], 0x0040), __byte_perm(bytes[14], bytes[15], 0x0040), 0x5410);
   return static_cast<uint32_t>(raw + 127);
+}
+
+// Per-warp block-column state: gamma^2 pairs in registers, Hessian in smem.
+template <int OBJ>
+__device__ __forceinline__ void load_column_state(const QuantParams& P, int64_t b, int lane, float* Hw,
+                                                  unsigned long long (&g2)[16]) {
+  if constexpr (OBJ == kObjGamma) {
+    const float4* gp = reinterpret_cast<const float4*>(P.gamma + b * kBlock);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 g = __ldg(gp + j);
+      g2[2 * j] = pack2(__fmul_rn(g.x, g.x), __fmul_rn(g.y, g.y));
+      g2[2 * j + 1] = pack2(__fmul_rn(g.z, g.z), __fmul_rn(g.w, g.w));
+    }
+  }
+  if constexpr (OBJ == kObjHess) {
+    __syncwarp();
+    const float4* src = reinterpret_cast<const float4*>(P.hessian + b * 1024);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) reinterpret_cast<float4*>(Hw)[lane + 32 * j] = __ldg(src + lane + 32 * j);
+    __syncwarp();
+  }
 }
 
 // --------------------------------------------------------------- TMA kernel
 
 template <int DT, int OBJ, int QM>
-__global__ void __launch_bounds__(kQuantThreads, 1)
+__global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F32) ? 1 : 2)
     quantize_tma_kernel(const __grid_constant__ CUtensorMap map, const QuantParams P) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  constexpr int kBoxesPerStage = (kTileBlocks * kBlock * Elem<DT>::kBytes) / 128;
-  constexpr int kStageBytes = kBoxesPerStage * kBoxBytes;
-  // 1024-byte alignment for the 128B-swizzle atoms.
+  constexpr int kStageBytes = Elem<DT>::kStageBytes;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
   float* Hs = reinterpret_cast<float*>(smem + kStages * kStageBytes);
@@ -369,10 +453,9 @@ __global__ void __launch_bounds__(kQuantThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int strip = blockIdx.x;
-  const int64_t col0 = static_cast<int64_t>(strip) * kTileBlocks * kBlock;
-  const int64_t boxes_left = (P.cols - col0 + (128 / Elem<DT>::kBytes) - 1) / (128 / Elem<DT>::kBytes);
-  const int boxes = boxes_left < kBoxesPerStage ? static_cast<int>(boxes_left) : kBoxesPerStage;
+  // This CTA's contiguous range of tiles, strip-major.
+  const int64_t t_begin = P.n_tiles * blockIdx.x / gridDim.x;
+  const int64_t t_end = P.n_tiles * (blockIdx.x + 1) / gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -380,16 +463,6 @@ __global__ void __launch_bounds__(kQuantThreads, 1)
       mbar_init(&empty[s], kConsumerWarps);
     }
     fence_mbar_init();
-  }
-  if constexpr (OBJ == kObjHess) {
-    // Stage the 8 block Hessians of this column strip (4 KB each).
-    const int64_t b0 = static_cast<int64_t>(strip) * kTileBlocks;
-    for (int i = threadIdx.x; i < kTileBlocks * 256; i += blockDim.x) {
-      const int blk = i >> 8;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (b0 + blk < P.nb) v = reinterpret_cast<const float4*>(P.hessian + (b0 + blk) * 1024)[i & 255];
-      reinterpret_cast<float4*>(Hs)[i] = v;
-    }
   }
   __syncthreads();
 
@@ -399,7 +472,11 @@ __global__ void __launch_bounds__(kQuantThreads, 1)
       prefetch_tensormap(&map);
       int64_t issued = 0;
       bool ok = true;
-      for (int64_t rt = blockIdx.y; rt < P.n_row_tiles; rt += gridDim.y, ++issued) {
+      for (int64_t t = t_begin; t < t_end; ++t, ++issued) {
+        const int64_t strip = t / P.n_row_tiles, rt = t % P.n_row_tiles;
+        const int64_t col0 = strip * kTileBlocks * kBlock;
+        const int64_t left = (P.cols - col0 + Elem<DT>::kBoxCols - 1) / Elem<DT>::kBoxCols;
+        const int boxes = left < Elem<DT>::kBoxesPerStage ? static_cast<int>(left) : Elem<DT>::kBoxesPerStage;
         const int s = static_cast<int>(issued % kStages);
         if (issued >= kStages && !mbar_wait(&empty[s], static_cast<uint32_t>((issued / kStages - 1) & 1))) {
           ok = false;
@@ -408,8 +485,7 @@ __global__ void __launch_bounds__(kQuantThreads, 1)
         mbar_arrive_expect_tx(&full[s], boxes * kBoxBytes);
         for (int k = 0; k < boxes; ++k)
           tma_load_2d(stages + s * kStageBytes + k * kBoxBytes, &map, &full[s],
-                      static_cast<int32_t>(col0 + k * (128 / Elem<DT>::kBytes)),
-                      static_cast<int32_t>(rt * kTileRows));
+                      static_cast<int32_t>(col0 + k * Elem<DT>::kBoxCols), static_cast<int32_t>(rt * kTileRows));
       }
       // Never leave with copies in flight: wait for the last issued stages.
       for (int64_t i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
@@ -421,24 +497,21 @@ __global__ void __launch_bounds__(kQuantThreads, 1)
   }
 
   // ---------------- consumer warps: warp w owns block column strip*8 + w.
-  const int64_t b = static_cast<int64_t>(strip) * kTileBlocks + warp;
-  const bool valid_col = b < P.nb;
   unsigned long long g2[16];
-  if constexpr (OBJ == kObjGamma) {
-    if (valid_col) {
-      const float4* gp = reinterpret_cast<const float4*>(P.gamma + b * kBlock);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 g = __ldg(gp + j);
-        g2[2 * j] = pack2(__fmul_rn(g.x, g.x), __fmul_rn(g.y, g.y));
-        g2[2 * j + 1] = pack2(__fmul_rn(g.z, g.z), __fmul_rn(g.w, g.w));
-      }
-    }
-  }
-  const float* Hb = Hs + warp * 1024;
+  float* Hw = Hs + warp * 1024;
+  int64_t cur_strip = -1;
+  bool valid_col = false;
+  int64_t b = 0;
   bool any_nonfinite = false;
   int64_t it = 0;
-  for (int64_t rt = blockIdx.y; rt < P.n_row_tiles; rt += gridDim.y, ++it) {
+  for (int64_t t = t_begin; t < t_end; ++t, ++it) {
+    const int64_t strip = t / P.n_row_tiles, rt = t % P.n_row_tiles;
+    if (strip != cur_strip) {
+      cur_strip = strip;
+      b = strip * kTileBlocks + warp;
+      valid_col = b < P.nb;
+      if (valid_col) load_column_state<OBJ>(P, b, lane, Hw, g2);
+    }
     const int s = static_cast<int>(it % kStages);
     // Warp-uniform verdict: a lane that timed out takes the whole warp out.
     if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>((it / kStages) & 1)))) {
@@ -447,16 +520,14 @@ __global__ void __launch_bounds__(kQuantThreads, 1)
     }
     const int64_t r = rt * kTileRows + lane;
     if (valid_col) {
-      unsigned long long t2[16];
-      float amax, second;
-      bool nonfinite;
-      read_block_smem<DT, QM>(stages + s * kStageBytes, warp, lane, t2, amax, second, nonfinite);
+      BlockData<DT> B;
+      read_block_smem<DT, QM>(stages + s * kStageBytes, warp, lane, B);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
       if (r < P.rows) {
-        any_nonfinite |= nonfinite;
+        any_nonfinite |= B.nonfinite;
         uint4 pk;
-        const uint32_t sc = quantize_one_block<OBJ, QM>(t2, amax, second, P, g2, Hb, pk);
+        const uint32_t sc = quantize_one_block<DT, OBJ, QM, true>(B, P, g2, Hw, pk);
         *reinterpret_cast<uint4*>(P.packed + r * (P.cols / 2) + b * 16) = pk;
         P.scales[r * P.nb + b] = static_cast<uint8_t>(sc);
       }
@@ -480,8 +551,7 @@ __global__ void __launch_bounds__(128) quantize_plain_kernel(const void* __restr
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = idx / P.nb, b = idx % P.nb;
-    unsigned long long t2[16];
-    uint32_t m1 = 0, m2 = 0;
+    BlockData<MXW_F32> B;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       float x0, x1;
@@ -498,14 +568,11 @@ __global__ void __launch_bounds__(128) quantize_plain_kernel(const void* __restr
         x0 = p[0];
         x1 = p[1];
       }
-      t2[j] = pack2(x0, x1);
-      const uint32_t a0 = f32_bits(x0) & 0x7fffffffu, a1 = f32_bits(x1) & 0x7fffffffu;
-      m2 = max(m2, min(m1, a0));
-      m1 = max(m1, a0);
-      m2 = max(m2, min(m1, a1));
-      m1 = max(m1, a1);
+      B.t2[j] = pack2(x0, x1);
     }
-    any_nonfinite |= m1 >= 0x7f800000u;
+    // Order statistics on fp32 magnitude bits (exact for every input type).
+    finish_stats_f32<MXW_F32, kQTop2>(B, B.t2);
+    any_nonfinite |= B.nonfinite;
     unsigned long long g2[16];
     if constexpr (OBJ == kObjGamma) {
 #pragma unroll
@@ -515,8 +582,8 @@ __global__ void __launch_bounds__(128) quantize_plain_kernel(const void* __restr
       }
     }
     uint4 pk;
-    const uint32_t sc = quantize_one_block<OBJ, QM>(t2, bits_f32(m1), bits_f32(m2), P, g2,
-                                                    P.hessian ? P.hessian + b * 1024 : nullptr, pk);
+    const uint32_t sc =
+        quantize_one_block<MXW_F32, OBJ, QM, false>(B, P, g2, P.hessian ? P.hessian + b * 1024 : nullptr, pk);
     uint8_t* dst = P.packed + r * (P.cols / 2) + b * 16;
     const uint32_t words[4] = {pk.x, pk.y, pk.z, pk.w};
 #pragma unroll
@@ -528,31 +595,49 @@ __global__ void __launch_bounds__(128) quantize_plain_kernel(const void* __restr
 
 // --------------------------------------------------------------- host side
 
+// Launch geometry per (kernel, device), computed once.
+struct LaunchInfo {
+  int per_sm = 0;
+  bool smem_set = false;
+};
+
+static LaunchInfo& launch_info(const void* kern, int dev) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, LaunchInfo> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const uint64_t key = reinterpret_cast<uint64_t>(kern) ^ (static_cast<uint64_t>(dev) << 56);
+  return cache[key];
+}
+
 template <int DT, int OBJ, int QM>
-static int launch_tma(const void* w, int64_t ld, const QuantParams& P, cudaStream_t stream) {
-  constexpr int kBoxCols = 128 / Elem<DT>::kBytes;
-  constexpr int kStageBytes = (kTileBlocks * kBlock * Elem<DT>::kBytes / 128) * kBoxBytes;
-  const size_t smem = 1024 + kStages * kStageBytes + (OBJ == kObjHess ? kTileBlocks * 4096 : 0) +
+static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStream_t stream) {
+  const size_t smem = 1024 + kStages * Elem<DT>::kStageBytes + (OBJ == kObjHess ? kTileBlocks * 4096 : 0) +
                       2 * kStages * sizeof(uint64_t);
   CUtensorMap map;
   const CUtensorMapDataType dt = DT == MXW_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : DT == MXW_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  if (make_tensor_map_2d(&map, dt, w, P.cols, P.rows, ld * Elem<DT>::kBytes, kBoxCols, kTileRows,
+  if (make_tensor_map_2d(&map, dt, w, P0.cols, P0.rows, ld * Elem<DT>::kBytes, Elem<DT>::kBoxCols, kTileRows,
                          CU_TENSOR_MAP_SWIZZLE_128B) != MXW_OK)
     return MXW_ECUDA;
   auto kern = quantize_tma_kernel<DT, OBJ, QM>;
-  int rc = set_max_smem(reinterpret_cast<const void*>(kern), smem);
-  if (rc != MXW_OK) return rc;
-  const int strips = static_cast<int>((P.nb + kTileBlocks - 1) / kTileBlocks);
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kQuantThreads, smem) != cudaSuccess || per_sm < 1)
-    per_sm = 1;
-  const int64_t want = static_cast<int64_t>(num_sms()) * per_sm;
-  int64_t splits = (want + strips - 1) / strips;
-  splits = std::max<int64_t>(1, std::min<int64_t>(splits, P.n_row_tiles));
-  dim3 grid(strips, static_cast<unsigned>(splits));
-  kern<<<grid, kQuantThreads, smem, stream>>>(map, P);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  LaunchInfo& li = launch_info(reinterpret_cast<const void*>(kern), dev);
+  if (!li.smem_set) {
+    const int rc = set_max_smem(reinterpret_cast<const void*>(kern), smem);
+    if (rc != MXW_OK) return rc;
+    int per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kQuantThreads, smem) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    li.per_sm = per_sm;
+    li.smem_set = true;
+  }
+  QuantParams P = P0;
+  P.n_tiles = ((P.nb + kTileBlocks - 1) / kTileBlocks) * P.n_row_tiles;
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(P.n_tiles, static_cast<int64_t>(num_sms()) * li.per_sm));
+  kern<<<static_cast<unsigned>(ctas), kQuantThreads, smem, stream>>>(map, P);
   return check_launch();
 }
 
@@ -625,6 +710,8 @@ extern "C" int mxw_quantize_mxfp4(const void* weight, int dtype, int64_t rows, i
   P.scales = scales;
   P.flags = flags;
   P.depth = mse_clip_depth;
+  P.zero = 0.0f;
+  P.negzero = -0.0f;
   // torch.quantile(|b|, p/100) over 32 values: ranks = fp32(p/100) * 31,
   // linear interpolation between the order statistics below and above.
   const float q = static_cast<float>(scale_percentile / 100.0);

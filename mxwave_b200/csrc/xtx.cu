@@ -1,0 +1,334 @@
+// K3: full X^T X of bf16 calibration activations on the tcgen05 tensor cores.
+//
+// G[i, j] += sum_n X[n, i] * X[n, j] for X [tokens, cols] row-major bf16.  As a
+// GEMM, M = N = cols and the reduction runs over tokens; both operands are
+// slices of X whose contiguous dimension is the output (MN) dimension, so they
+// are consumed "MN-major" straight from the TMA tiles -- no transpose pass.
+//
+// CTA tile 128 (i) x 256 (j), 64 tokens per pipeline stage:
+//   warp 0      TMA producer: A = X[n0:n0+64, i0:i0+128] (2 boxes of 64x64),
+//               B = X[n0:n0+64, j0:j0+256] (4 boxes), 128-byte swizzle
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer
+//               (kind::f16, bf16 x bf16 -> fp32, M=128 N=256 K=16, 4 per stage)
+//   warps 2..9  epilogue: each owns 32 TMEM lanes (rows) x 128 columns
+// Accuracy: the tensor core's fp32 accumulation is not round-to-nearest (its
+// error grows with the number of K steps in one accumulator).  So tokens are
+// accumulated in chunks of 256 (16 K steps) in one of two TMEM buffers (2 x
+// 256 columns); while the MMA warp fills one buffer, the epilogue warps add the
+// other into round-to-nearest fp32 totals held in registers.  The totals are
+// added into the caller's Gram once, at the end.
+// Shared-memory descriptors (MN-major, SWIZZLE_128B): the 16-byte-unit layout
+// is ((8, n), (8, k)) : ((1, LBO), (8, SBO)) -- 64 contiguous channels per
+// 128-byte row, LBO = bytes between 64-channel boxes, SBO = 1024 bytes
+// between groups of 8 tokens.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "runtime.h"
+#include "tma.cuh"
+
+namespace mxw {
+
+constexpr int kXtxBM = 128;
+constexpr int kXtxBN = 256;
+constexpr int kXtxBK = 64;  // tokens per stage
+constexpr int kXtxStages = 4;
+constexpr int kXtxBoxBytes = kXtxBK * 128;                    // 64 tokens x 64 channels bf16
+constexpr int kXtxABytes = (kXtxBM / 64) * kXtxBoxBytes;      // 16 KB
+constexpr int kXtxBBytes = (kXtxBN / 64) * kXtxBoxBytes;      // 32 KB
+constexpr int kXtxStageBytes = kXtxABytes + kXtxBBytes;       // 48 KB
+constexpr int kXtxEpiWarps = 8;
+constexpr int kXtxThreads = (2 + kXtxEpiWarps) * 32;
+constexpr int kXtxChunkStages = 4;  // 256 tokens per TMEM accumulation chunk
+constexpr uint32_t kXtxTmemCols = 512;  // two 128 x 256 fp32 accumulators
+constexpr int64_t kXtxMaxTokens = 262144;  // tokens per launch
+
+struct XtxParams {
+  int64_t tokens, cols, ldg, n_kblocks;
+  float* gram;
+  uint32_t* flags;
+};
+
+// ---------------------------------------------------------- tcgen05 helpers
+
+__device__ __forceinline__ uint64_t make_smem_desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3fff);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3fff) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3fff) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 A/B, fp32 D, both MN-major.
+__host__ __device__ constexpr uint32_t make_idesc_bf16_f32_mn(int m, int n) {
+  return (1u << 4)                                   // D format: f32
+         | (1u << 7)                                 // A format: bf16
+         | (1u << 10)                                // B format: bf16
+         | (1u << 15)                                // A major: MN
+         | (1u << 16)                                // B major: MN
+         | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_f32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 consecutive fp32 columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = __uint_as_float(r[k]);
+}
+
+// 32 lanes x 32 consecutive fp32 columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
+}
+
+// ------------------------------------------------------------------- kernel
+
+__global__ void __launch_bounds__(kXtxThreads, 1)
+    xtx_kernel(const __grid_constant__ CUtensorMap map, const XtxParams P) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kXtxStages * kXtxStageBytes);
+  uint64_t* empty = full + kXtxStages;
+  uint64_t* tfull = empty + kXtxStages;  // [2] accumulator buffer ready
+  uint64_t* tempty = tfull + 2;          // [2] accumulator buffer drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* fail = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i0 = static_cast<int64_t>(blockIdx.y) * kXtxBM;
+  const int64_t j0 = static_cast<int64_t>(blockIdx.x) * kXtxBN;
+  const int64_t n_chunks = (P.n_kblocks + kXtxChunkStages - 1) / kXtxChunkStages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kXtxStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kXtxEpiWarps);
+    }
+    *fail = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kXtxTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&map);
+      int64_t kb = 0;
+      bool ok = true;
+      for (; kb < P.n_kblocks; ++kb) {
+        const int s = static_cast<int>(kb % kXtxStages);
+        if (kb >= kXtxStages && !mbar_wait(&empty[s], static_cast<uint32_t>((kb / kXtxStages - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * kXtxStageBytes;
+        const int32_t y = static_cast<int32_t>(kb * kXtxBK);
+        mbar_arrive_expect_tx(&full[s], kXtxStageBytes);
+#pragma unroll
+        for (int q = 0; q < kXtxBM / 64; ++q)
+          tma_load_2d(st + q * kXtxBoxBytes, &map, &full[s], static_cast<int32_t>(i0 + 64 * q), y);
+#pragma unroll
+        for (int q = 0; q < kXtxBN / 64; ++q)
+          tma_load_2d(st + kXtxABytes + q * kXtxBoxBytes, &map, &full[s], static_cast<int32_t>(j0 + 64 * q), y);
+      }
+      for (int64_t j = (kb > kXtxStages ? kb - kXtxStages : 0); j < kb; ++j)
+        if (!mbar_wait(&full[j % kXtxStages], static_cast<uint32_t>((j / kXtxStages) & 1))) ok = false;
+      if (!ok) atomicOr(fail, 1);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32_mn(kXtxBM, kXtxBN);
+      bool ok = true;
+      int64_t kb = 0;
+      int64_t c = 0;
+      for (; c < n_chunks && ok; ++c) {
+        const int buf = static_cast<int>(c & 1);
+        if (c >= 2 && !mbar_wait(&tempty[buf], static_cast<uint32_t>((c / 2 - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * kXtxBN);
+        const int64_t kb_end = (c + 1) * kXtxChunkStages < P.n_kblocks ? (c + 1) * kXtxChunkStages : P.n_kblocks;
+        for (int64_t first = kb; kb < kb_end; ++kb) {
+          const int s = static_cast<int>(kb % kXtxStages);
+          if (!mbar_wait(&full[s], static_cast<uint32_t>((kb / kXtxStages) & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + s * kXtxStageBytes);
+          const uint32_t b_base = a_base + kXtxABytes;
+#pragma unroll
+          for (int kk = 0; kk < kXtxBK / 16; ++kk) {
+            // 16 tokens = two 8-row swizzle atoms = 2048 bytes further along K.
+            const uint64_t ad = make_smem_desc_mn_sw128(a_base + kk * 2048, kXtxBoxBytes, 1024);
+            const uint64_t bd = make_smem_desc_mn_sw128(b_base + kk * 2048, kXtxBoxBytes, 1024);
+            mma_bf16_f32(d_tmem, ad, bd, idesc, (kb > first || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);  // stage reusable once these MMAs have read it
+        }
+        mma_commit(&tfull[buf]);  // chunk accumulated (or nothing more in flight)
+      }
+      if (!ok) {
+        atomicOr(fail, 1);
+        // Let any epilogue warp still waiting on a chunk see it "ready" so the
+        // CTA unwinds; the fail flag keeps the data from being used.
+        for (; c < n_chunks; ++c) mma_commit(&tfull[c & 1]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int e = warp - 2;
+    const int quarter = warp & 3;     // TMEM lanes 32*quarter .. +31 (hardware rule)
+    const int half = e >> 2;          // columns 128*half .. +127 of the tile
+    float total[128];
+#pragma unroll
+    for (int k = 0; k < 128; ++k) total[k] = 0.0f;
+    bool ok = true;
+    for (int64_t c = 0; c < n_chunks; ++c) {
+      const int buf = static_cast<int>(c & 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], static_cast<uint32_t>((c / 2) & 1)))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t base = tmem + (static_cast<uint32_t>(32 * quarter) << 16) +
+                            static_cast<uint32_t>(buf * kXtxBN + 128 * half);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float v[16];
+        tmem_ld_32x32b_x16(base + static_cast<uint32_t>(16 * q), v);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) total[16 * q + k] = __fadd_rn(total[16 * q + k], v[k]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+    if (!ok) atomicOr(fail, 1);
+    // All epilogue warps agree before writing (named barrier 1, 256 threads).
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    if (*reinterpret_cast<volatile int*>(fail) == 0 && j0 + 128 * half < P.cols) {
+      float* grow = P.gram + (i0 + 32 * quarter + lane) * P.ldg + j0 + 128 * half;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        float4 o = reinterpret_cast<float4*>(grow)[k];
+        o.x = __fadd_rn(o.x, total[4 * k]);
+        o.y = __fadd_rn(o.y, total[4 * k + 1]);
+        o.z = __fadd_rn(o.z, total[4 * k + 2]);
+        o.w = __fadd_rn(o.w, total[4 * k + 3]);
+        reinterpret_cast<float4*>(grow)[k] = o;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kXtxTmemCols);
+  }
+  if (threadIdx.x == 0 && *fail && P.flags) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
+}
+
+}  // namespace mxw
+
+using namespace mxw;
+
+extern "C" int mxw_accumulate_xtx(const void* x, int64_t tokens, int64_t cols, int64_t ld, float* gram,
+                                  int64_t ldg, uint32_t* flags, void* stream) {
+  if (tokens < 0 || cols <= 0 || cols % 128 != 0 || ld < cols || ld % 8 != 0 || ldg < cols || ldg % 4 != 0)
+    return MXW_EINVAL;
+  if (tokens == 0) return MXW_OK;
+  if (!x || !gram) return MXW_EINVAL;
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(gram) % 16 != 0) return MXW_EINVAL;
+  if (tokens >= (int64_t(1) << 31) || cols >= (int64_t(1) << 31)) return MXW_EINVAL;
+  const size_t smem = 1024 + kXtxStages * kXtxStageBytes + (2 * kXtxStages + 4) * sizeof(uint64_t) + 16;
+  const int rc = set_max_smem(reinterpret_cast<const void*>(xtx_kernel), smem);
+  if (rc != MXW_OK) return rc;
+  // One launch per slice of at most kXtxMaxTokens tokens: every on-device wait
+  // stays far below the timeout, and each slice's TMEM accumulator is folded
+  // into the fp32 Gram before the next one starts.
+  dim3 grid(static_cast<unsigned>((cols + kXtxBN - 1) / kXtxBN), static_cast<unsigned>(cols / kXtxBM));
+  for (int64_t t0 = 0; t0 < tokens; t0 += kXtxMaxTokens) {
+    const int64_t n = std::min<int64_t>(kXtxMaxTokens, tokens - t0);
+    CUtensorMap map;
+    if (make_tensor_map_2d(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<const uint16_t*>(x) + t0 * ld, cols,
+                           n, ld * 2, 64, kXtxBK, CU_TENSOR_MAP_SWIZZLE_128B) != MXW_OK)
+      return MXW_ECUDA;
+    XtxParams P{};
+    P.tokens = n;
+    P.cols = cols;
+    P.ldg = ldg;
+    P.n_kblocks = (n + kXtxBK - 1) / kXtxBK;
+    P.gram = gram;
+    P.flags = flags;
+    xtx_kernel<<<grid, kXtxThreads, smem, static_cast<cudaStream_t>(stream)>>>(map, P);
+    const int st = check_launch();
+    if (st != MXW_OK) return st;
+  }
+  return MXW_OK;
+}

@@ -39,6 +39,23 @@ def _gpu(w, dev, **kw):
     return p.cpu().numpy(), s.cpu().numpy()
 
 
+def assert_same_bytes(weight: np.ndarray, p, s, p_ref, s_ref) -> None:
+    """Bit-exact comparison with a readable report of the first mismatches."""
+    bad_s = np.argwhere(s != s_ref)
+    bad_p = np.argwhere(p != p_ref)
+    if bad_s.size == 0 and bad_p.size == 0:
+        return
+    lines = [f"{len(bad_s)} scale and {len(bad_p)} packed byte mismatches"]
+    w = weight if weight.dtype == np.float32 else syn.bf16_bits_to_f32(weight)
+    for r, b in bad_s[:5]:
+        blk = w[r, 32 * b: 32 * b + 32]
+        lines.append(f"scale[{r},{b}] got {s[r, b]} want {s_ref[r, b]} block {blk.tolist()}")
+    for r, c in bad_p[:8]:
+        vals = "" if w is None else f" inputs {w[r, 2 * c]!r}, {w[r, 2 * c + 1]!r}"
+        lines.append(f"packed[{r},{c}] got {p[r, c]:#04x} want {p_ref[r, c]:#04x} scale {s_ref[r, (2 * c) // 32]}{vals}")
+    raise AssertionError("\n".join(lines))
+
+
 @pytest.mark.parametrize("case", CASES, ids=[c.name for c in CASES])
 def test_golden_case_bit_exact(case, cuda_device) -> None:
     w = _to_device(case.weight, cuda_device)
@@ -48,8 +65,7 @@ def test_golden_case_bit_exact(case, cuda_device) -> None:
     if case.hessian is not None:
         kw["hessian"] = torch.from_numpy(case.hessian).to(cuda_device)
     p, s = _gpu(w, cuda_device, **kw)
-    np.testing.assert_array_equal(s, case.scales)
-    np.testing.assert_array_equal(p, case.packed)
+    assert_same_bytes(case.weight, p, s, case.packed, case.scales)
 
 
 def _bf16_all_finite_blocks() -> np.ndarray:
@@ -72,8 +88,7 @@ def test_every_bf16_value_matches_oracle(kw, cuda_device) -> None:
     for arr in (w, shuffled):
         p, s = _gpu(_to_device(arr, cuda_device), cuda_device, **kw)
         po, so = oracle.quantize_mxfp4(arr, **kw)
-        np.testing.assert_array_equal(s, so)
-        np.testing.assert_array_equal(p, po)
+        assert_same_bytes(syn.bf16_bits_to_f32(arr), p, s, po, so)
 
 
 SHAPES = [(1, 32), (7, 64), (31, 96), (33, 160), (64, 544), (100, 2048), (257, 768), (40, 5120)]

@@ -105,9 +105,12 @@ def test_finalize_moments(cuda_device) -> None:
     assert lib.mxw_finalize_moments(s1.data_ptr(), s2.data_ptr(), 333, 77, ma.data_ptr(), rms.data_ptr(),
                                     _stream(cuda_device)) == 0
     torch.cuda.synchronize()
-    # Same fp32 operations as the reference's finalize (calibration.py:262-266).
-    assert torch.equal(ma, s1 / 77)
-    assert torch.equal(rms, torch.sqrt(s2 / 77))
+    # Same fp32 operations as the reference's CPU finalize (calibration.py:
+    # 262-266): IEEE division by the count, then an IEEE square root.
+    c1, c2 = s1.cpu(), s2.cpu()
+    assert torch.equal(ma.cpu(), c1 / 77)
+    # torch's vectorised CPU sqrt may differ from the IEEE square root by 1 ulp.
+    torch.testing.assert_close(rms.cpu(), torch.sqrt(c2 / 77), rtol=2e-7, atol=0)
 
 
 def test_dequant_matches_oracle(cuda_device) -> None:
@@ -119,3 +122,40 @@ def test_dequant_matches_oracle(cuda_device) -> None:
     d = dequant_mxfp4(p, s, (33, 256)).cpu().numpy()
     ref = oracle.dequant_mxfp4(p.cpu().numpy(), s.cpu().numpy(), 256)
     np.testing.assert_array_equal(d, ref)
+
+
+# ------------------------------------------------------------- full X^T X
+
+
+def _full_err(got: np.ndarray, ref: np.ndarray) -> float:
+    d = np.diag(ref)
+    scale = np.sqrt(np.maximum(np.outer(d, d), 1e-300))
+    return float(np.max(np.abs(got - ref) / scale))
+
+
+@pytest.mark.parametrize("tokens,cols", [(1, 128), (64, 128), (1000, 256), (4097, 640), (65536, 1024)])
+def test_xtx_matches_fp64(tokens, cols, cuda_device) -> None:
+    lib = _lib.load()
+    x, xf = _x(tokens, cols, tokens * 3 + cols, cuda_device)
+    g = torch.zeros(cols, cols, device=cuda_device)
+    st = lib.mxw_accumulate_xtx(x.data_ptr(), tokens, cols, cols, g.data_ptr(), cols, None, _stream(cuda_device))
+    assert st == _lib.MXW_OK
+    torch.cuda.synchronize()
+    ref = oracle.gram(xf)
+    assert _full_err(g.cpu().numpy().astype(np.float64), ref) < RTOL
+
+
+def test_xtx_accumulates_with_strides(cuda_device) -> None:
+    lib = _lib.load()
+    x, xf = _x(3000, 520, 12, cuda_device)
+    xs = x[:, :512]  # row stride 520 elements (1040 bytes, 16-byte multiple)
+    g = torch.zeros(512, 520, device=cuda_device)  # Gram row stride 520
+    g[:, :512] = torch.eye(512, device=cuda_device)
+    for a, b in ((0, 1234), (1234, 3000)):
+        part = xs[a:b]
+        assert lib.mxw_accumulate_xtx(part.data_ptr(), b - a, 512, 520, g.data_ptr(), 520, None,
+                                      _stream(cuda_device)) == 0
+    torch.cuda.synchronize()
+    ref = oracle.gram(xf[:, :512]) + np.eye(512)
+    assert _full_err(g[:, :512].cpu().numpy().astype(np.float64), ref) < RTOL
+    assert float(g[:, 512:].abs().max()) == 0.0  # padding columns untouched
