@@ -10,8 +10,9 @@
 //     chain over s = 0..31.
 // The unweighted and gamma errors only need dW^2, so they are evaluated on
 // magnitudes: |dW| = q(|t|/2^e) * 2^e - |t|.  Per element pair and candidate:
-// one packed multiply, one E2M1 conversion (XU pipe), two byte permutes that
-// decode the codes to an exact f16x2, and packed fp32 FMA / multiply / add.
+// one packed multiply, the E2M1 round trip (cvt to e2m1x2, cvt back to an
+// exact f16x2 in the same asm block), two f16->f32 conversions, and packed
+// fp32 FMA / multiply / add.
 //
 // Data layout: one thread owns one 32-element block.  A warp owns one block
 // column and 32 consecutive rows, so gamma and the block's 32x32 Hessian are
@@ -22,7 +23,9 @@
 // consumer warps.  A tile is 32 rows x 256 columns (8 block columns) loaded by
 // TMA with the 128-byte swizzle into a ring of shared-memory stages; with the
 // swizzle, the 8 lanes of a shared-memory phase (8 consecutive rows, same
-// chunk) hit 8 distinct bank groups.
+// chunk) hit 8 distinct bank groups.  Outputs go the same way in reverse: each
+// thread writes its 16 packed bytes into a swizzled 32 x 128-byte staging tile,
+// one TMA store writes the tile, and one warp writes the 32 x 8 scale bytes.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -40,9 +43,17 @@ namespace mxw {
 constexpr int kTileRows = 32;
 constexpr int kTileBlocks = 8;
 constexpr int kConsumerWarps = kTileBlocks;
-constexpr int kQuantThreads = (kConsumerWarps + 1) * 32;
+constexpr int kProducerWarp = kConsumerWarps;      // TMA loads
+constexpr int kStoreWarp = kConsumerWarps + 1;     // TMA stores of packed bytes + scale rows
+constexpr int kQuantThreads = (kConsumerWarps + 2) * 32;
 constexpr int kStages = 4;
 constexpr int kBoxBytes = kTileRows * 128;  // one TMA box: 32 rows x 128 bytes
+constexpr int kOutTileBytes = kTileRows * kTileBlocks * 16;  // packed bytes of one tile (32 x 128)
+constexpr int kScaleTileBytes = kTileRows * kTileBlocks;      // scale bytes of one tile (32 x 8)
+// Output staging ring: consumers fill a buffer and arrive on out_full; the store
+// warp writes it out and, once the TMA store no longer reads it, arrives on
+// out_empty.  No barrier couples the consumer warps to each other.
+constexpr int kOutBuffers = 4;
 
 enum Obj { kObjNone = 0, kObjGamma = 1, kObjHess = 2, kObjRtn = 3 };
 enum QMode { kQAmax = 0, kQTop2 = 1, kQGeneral = 2 };
@@ -217,30 +228,34 @@ __device__ __forceinline__ float kth_magnitude(const unsigned long long (&nt2)[1
 // product q*2^e is exact, so the fused form rounds like the reference's
 // separate multiply and subtract, except when q*2^e overflows (e >= 126),
 // which takes the unfused path.
+template <bool UNFUSED>
 __device__ __forceinline__ unsigned long long abs_dw2(unsigned long long nt, unsigned long long NI2,
-                                                      unsigned long long S2, bool unfused,
-                                                      unsigned long long NZ2) {
+                                                      unsigned long long S2, unsigned long long NZ2) {
   const f2 x = unpack2(mul2(nt, NI2));  // |t| / 2^e exactly (NI2 = -2^-e)
-  const unsigned long long q = e2m1_mag_to_f32x2(e2m1x2(x.x, x.y));
-  return unfused ? add2(mul2_rounded(q, S2, NZ2), nt) : fma2(q, S2, nt);
+  uint32_t h2;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(h2) : "f"(x.y), "f"(x.x));
+  const __half2 hh = *reinterpret_cast<const __half2*>(&h2);
+  const unsigned long long q = pack2(__low2float(hh), __high2float(hh));
+  if constexpr (UNFUSED) return add2(mul2_rounded(q, S2, NZ2), nt);
+  return fma2(q, S2, nt);
 }
 
 // Unweighted / gamma error of one candidate exponent e: mean over the block of
 // dW^2 (times gamma^2), core.py:224-234.
-template <bool GAMMA>
+template <bool GAMMA, bool UNFUSED>
 __device__ __forceinline__ float candidate_error(const unsigned long long (&nt2)[16], int e,
                                                  const unsigned long long (&g2)[16], unsigned long long NZ2) {
   const float s = exp2i(e);
   const float ninv = -exp2i(-e);
   const unsigned long long S2 = pack2(s, s), NI2 = pack2(ninv, ninv);
-  const bool unfused = e >= 126;
   unsigned long long p[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
 #pragma unroll
     for (int lp = 0; lp < 4; ++lp) {
       const int j = q * 4 + lp;
-      const unsigned long long d = abs_dw2(nt2[j], NI2, S2, unfused, NZ2);
+      const unsigned long long d = abs_dw2<UNFUSED>(nt2[j], NI2, S2, NZ2);
       // fl(dW^2), then fl(fl(dW^2) * gamma^2): each product rounded before the add.
       unsigned long long sq = mul2_rounded(d, d, NZ2);
       if constexpr (GAMMA) sq = mul2_rounded(sq, g2[j], NZ2);
@@ -276,17 +291,16 @@ __device__ __forceinline__ ulonglong2 load_h16(const float* p) {
   return v;
 }
 
-template <int DT, bool HS_SHARED>
+template <int DT, bool HS_SHARED, bool UNFUSED>
 __device__ __forceinline__ float candidate_error_hessian(const BlockData<DT>& B, int e, const float* Hs,
                                                          unsigned long long NZ2) {
   const float s = exp2i(e);
   const float ninv = -exp2i(-e);
   const unsigned long long S2 = pack2(s, s), NI2 = pack2(ninv, ninv);
-  const bool unfused = e >= 126;
   unsigned long long w[16];
 #pragma unroll
   for (int sp = 0; sp < 16; ++sp) {
-    const f2 d = unpack2(abs_dw2(B.nt2[sp], NI2, S2, unfused, NZ2) ^ B.sign_pair(sp));
+    const f2 d = unpack2(abs_dw2<UNFUSED>(B.nt2[sp], NI2, S2, NZ2) ^ B.sign_pair(sp));
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int si = 2 * sp + h;
@@ -311,7 +325,7 @@ __device__ __forceinline__ float candidate_error_hessian(const BlockData<DT>& B,
 #pragma unroll
     for (int lp = 0; lp < 4; ++lp) {
       const int j = q * 4 + lp;
-      const unsigned long long d = abs_dw2(B.nt2[j], NI2, S2, unfused, NZ2) ^ B.sign_pair(j);
+      const unsigned long long d = abs_dw2<UNFUSED>(B.nt2[j], NI2, S2, NZ2) ^ B.sign_pair(j);
       const unsigned long long prod = mul2_rounded(w[j], d, NZ2);
       p[lp] = (q == 0) ? prod : add2(p[lp], prod);
     }
@@ -386,11 +400,15 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
     const bool safe_new = safe_e < lo_e || safe_e > hi_e;
     for (int k = 0; k < n_seq + (safe_new ? 1 : 0); ++k) {
       const int e = k < n_seq ? lo_e + k : safe_e;
+      // q * 2^e can overflow only for e >= 126: that rare case takes the
+      // unfused multiply-then-subtract form (a block-uniform branch).
       float err;
       if constexpr (OBJ == kObjHess) {
-        err = candidate_error_hessian<DT, HS_SHARED>(B, e, Hs, NZ2);
+        err = e < 126 ? candidate_error_hessian<DT, HS_SHARED, false>(B, e, Hs, NZ2)
+                      : candidate_error_hessian<DT, HS_SHARED, true>(B, e, Hs, NZ2);
       } else {
-        err = candidate_error<OBJ == kObjGamma>(B.nt2, e, g2, NZ2);
+        err = e < 126 ? candidate_error<OBJ == kObjGamma, false>(B.nt2, e, g2, NZ2)
+                      : candidate_error<OBJ == kObjGamma, true>(B.nt2, e, g2, NZ2);
       }
       if (err < best) raw = e;
       best = (isnan(err) || isnan(best)) ? __int_as_float(0x7fffffff) : fminf(best, err);
@@ -441,15 +459,20 @@ __device__ __forceinline__ void load_column_state(const QuantParams& P, int64_t 
 
 template <int DT, int OBJ, int QM>
 __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F32) ? 1 : 2)
-    quantize_tma_kernel(const __grid_constant__ CUtensorMap map, const QuantParams P) {
+    quantize_tma_kernel(const __grid_constant__ CUtensorMap map, const __grid_constant__ CUtensorMap out_map,
+                        const QuantParams P) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   constexpr int kStageBytes = Elem<DT>::kStageBytes;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
-  float* Hs = reinterpret_cast<float*>(smem + kStages * kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes +
+  uint8_t* out_stage = smem + kStages * kStageBytes;               // [ring][32 rows][128 B], 128B-swizzled
+  uint8_t* scale_stage = out_stage + kOutBuffers * kOutTileBytes;  // [ring][32 rows][8 B]
+  float* Hs = reinterpret_cast<float*>(scale_stage + kOutBuffers * kScaleTileBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(Hs) +
                                                (OBJ == kObjHess ? kTileBlocks * 1024 * 4 : 0));
   uint64_t* empty = full + kStages;
+  uint64_t* out_full = empty + kStages;
+  uint64_t* out_empty = out_full + kOutBuffers;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -462,11 +485,57 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    for (int i = 0; i < kOutBuffers; ++i) {
+      mbar_init(&out_full[i], kConsumerWarps);
+      mbar_init(&out_empty[i], 1);
+    }
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
+  if (warp == kStoreWarp) {
+    // ---------------- store warp: one TMA store + 32 scale rows per tile.
+    bool ok = true;
+    int64_t it = 0;
+    const bool scale_words = (P.nb % 8 == 0) && (reinterpret_cast<uintptr_t>(P.scales) % 8 == 0);
+    for (int64_t t = t_begin; t < t_end; ++t, ++it) {
+      const int64_t strip = t / P.n_row_tiles, rt = t % P.n_row_tiles;
+      const int buf = static_cast<int>(it % kOutBuffers);
+      if (!__all_sync(0xffffffffu, mbar_wait(&out_full[buf], static_cast<uint32_t>((it / kOutBuffers) & 1)))) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) {
+        tma_store_2d(&out_map, out_stage + buf * kOutTileBytes, static_cast<int32_t>(strip * kTileBlocks * 16),
+                     static_cast<int32_t>(rt * kTileRows));
+        bulk_commit_group();
+      }
+      const uint8_t* sstage = scale_stage + buf * kScaleTileBytes;
+      const int64_t r = rt * kTileRows + lane;
+      const int64_t b0 = strip * kTileBlocks;
+      if (r < P.rows) {
+        if (scale_words && b0 + kTileBlocks <= P.nb) {
+          *reinterpret_cast<uint2*>(P.scales + r * P.nb + b0) = *reinterpret_cast<const uint2*>(sstage + lane * kTileBlocks);
+        } else {
+          for (int k = 0; k < kTileBlocks && b0 + k < P.nb; ++k) P.scales[r * P.nb + b0 + k] = sstage[lane * kTileBlocks + k];
+        }
+      }
+      __syncwarp();
+      // Release the buffer stored kOutBuffers-1 tiles ago: at most
+      // kOutBuffers-1 stores may still read shared memory.
+      if (lane == 0) {
+        bulk_wait_group_read<kOutBuffers - 1>();
+        if (it >= kOutBuffers - 1) mbar_arrive(&out_empty[(it - (kOutBuffers - 1)) % kOutBuffers]);
+      }
+    }
+    if (lane == 0) {
+      bulk_wait_group_all();
+      if (!ok && P.flags) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
+    }
+    return;
+  }
+
+  if (warp == kProducerWarp) {
     // ---------------- producer warp: one elected lane issues all TMA loads.
     if (lane == 0) {
       prefetch_tensormap(&map);
@@ -518,23 +587,36 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       if (P.flags && lane == 0) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
       break;
     }
-    const int64_t r = rt * kTileRows + lane;
+    const int buf = static_cast<int>(it % kOutBuffers);
+    uint8_t* ostage = out_stage + buf * kOutTileBytes;
+    uint8_t* sstage = scale_stage + buf * kScaleTileBytes;
+    uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t sc = 0;
     if (valid_col) {
       BlockData<DT> B;
       read_block_smem<DT, QM>(stages + s * kStageBytes, warp, lane, B);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      if (r < P.rows) {
+      if (rt * kTileRows + lane < P.rows) {
         any_nonfinite |= B.nonfinite;
-        uint4 pk;
-        const uint32_t sc = quantize_one_block<DT, OBJ, QM, true>(B, P, g2, Hw, pk);
-        *reinterpret_cast<uint4*>(P.packed + r * (P.cols / 2) + b * 16) = pk;
-        P.scales[r * P.nb + b] = static_cast<uint8_t>(sc);
+        sc = quantize_one_block<DT, OBJ, QM, true>(B, P, g2, Hw, pk);
       }
     } else {
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
+    // Stage: row `lane`, 16-byte chunk `warp`, 128B-swizzled (chunk ^ row%8)
+    // to match the output tensor map.  Wait for the buffer to be free first.
+    if (it >= kOutBuffers &&
+        !__all_sync(0xffffffffu, mbar_wait(&out_empty[buf], static_cast<uint32_t>((it / kOutBuffers - 1) & 1)))) {
+      if (P.flags && lane == 0) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
+      break;
+    }
+    *reinterpret_cast<uint4*>(ostage + lane * 128 + ((warp ^ (lane & 7)) << 4)) = pk;
+    sstage[lane * kTileBlocks + warp] = static_cast<uint8_t>(sc);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&out_full[buf]);
   }
   if (P.flags && __any_sync(0xffffffffu, any_nonfinite) && lane == 0) atomicOr(P.flags, MXW_FLAG_NONFINITE);
 }
@@ -611,14 +693,18 @@ static LaunchInfo& launch_info(const void* kern, int dev) {
 
 template <int DT, int OBJ, int QM>
 static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStream_t stream) {
-  const size_t smem = 1024 + kStages * Elem<DT>::kStageBytes + (OBJ == kObjHess ? kTileBlocks * 4096 : 0) +
-                      2 * kStages * sizeof(uint64_t);
+  const size_t smem = 1024 + kStages * Elem<DT>::kStageBytes + kOutBuffers * (kOutTileBytes + kScaleTileBytes) +
+                      (OBJ == kObjHess ? kTileBlocks * 4096 : 0) + (2 * kStages + 2 * kOutBuffers) * sizeof(uint64_t);
   CUtensorMap map;
   const CUtensorMapDataType dt = DT == MXW_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : DT == MXW_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   if (make_tensor_map_2d(&map, dt, w, P0.cols, P0.rows, ld * Elem<DT>::kBytes, Elem<DT>::kBoxCols, kTileRows,
                          CU_TENSOR_MAP_SWIZZLE_128B) != MXW_OK)
+    return MXW_ECUDA;
+  CUtensorMap out_map;
+  if (make_tensor_map_2d(&out_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, P0.packed, P0.cols / 2, P0.rows, P0.cols / 2,
+                         kTileBlocks * 16, kTileRows, CU_TENSOR_MAP_SWIZZLE_128B) != MXW_OK)
     return MXW_ECUDA;
   auto kern = quantize_tma_kernel<DT, OBJ, QM>;
   int dev = 0;
@@ -637,7 +723,7 @@ static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStre
   QuantParams P = P0;
   P.n_tiles = ((P.nb + kTileBlocks - 1) / kTileBlocks) * P.n_row_tiles;
   const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(P.n_tiles, static_cast<int64_t>(num_sms()) * li.per_sm));
-  kern<<<static_cast<unsigned>(ctas), kQuantThreads, smem, stream>>>(map, P);
+  kern<<<static_cast<unsigned>(ctas), kQuantThreads, smem, stream>>>(map, out_map, P);
   return check_launch();
 }
 
