@@ -32,6 +32,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 TOKENS, HIDDEN, INTER = 8192, 5120, 17408
+XTX_TOKENS = 65536
 N_WEIGHTS = 2
 DEPTH = 1
 PCT = 99.5
@@ -51,6 +52,16 @@ def _peaks() -> tuple[float, str]:
         except (KeyError, ValueError):
             pass
     return 6650.0, "fallback"
+
+
+def _peaks_tensor() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured dense bf16 (burst)"
+        except (KeyError, ValueError):
+            pass
+    return 1590.0, "fallback dense bf16"
 
 
 class ClockSampler:
@@ -175,6 +186,8 @@ def run_ours(args) -> None:
 
     # ---- end to end through the public API, host pinned buffers.
     e2e = run_e2e(args, dev, world, rank)
+    # ---- calibration: X^T X on the tensor cores (config 3's token set).
+    xtx = None if args.no_xtx else run_xtx(args, dev, world, rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -210,6 +223,7 @@ def run_ours(args) -> None:
                      "bytes_per_launch": int(bytes_per_launch), "avg_launch_ms": round(q_ms, 4)},
         "e2e": e2e,
         "cpu_baseline": cpu,
+        "calibration_xtx": xtx,
         "gpu_launches": 4 * args.steps,
         "clocks": clocks.summary(),
     }
@@ -217,18 +231,24 @@ def run_ours(args) -> None:
 
 
 def run_e2e(args, dev, world: int, rank: int) -> dict:
-    """Same step through the public API with pinned host inputs and outputs."""
+    """Same step through the public API from pinned host memory to pinned host memory.
+
+    ActivationCollector (moments kernel) on the host activations, then the
+    ChunkStreamer (H2D / quantize / D2H overlapped on three streams) for both
+    weights; the timed region holds every host<->device copy of the step.
+    """
     import torch
 
     from mxwave_b200 import synthetic
     from mxwave_b200.calibration import ActivationCollector
-    from mxwave_b200.core import quantize_mxfp4
+    from mxwave_b200.streamer import ChunkStreamer
 
     x_h = synthetic.torch_activations(TOKENS, HIDDEN, seed=7 + rank, device=dev).cpu().pin_memory()
     w_h = [synthetic.torch_dense_weight(INTER, HIDDEN, seed=70 + i + rank, device=dev, sigma=0.015,
                                         outlier_fraction=0.0).cpu().pin_memory() for i in range(N_WEIGHTS)]
     p_h = [torch.empty((INTER, HIDDEN // 2), dtype=torch.uint8).pin_memory() for _ in range(N_WEIGHTS)]
     s_h = [torch.empty((INTER, HIDDEN // 32), dtype=torch.uint8).pin_memory() for _ in range(N_WEIGHTS)]
+    streamer = ChunkStreamer(dev)
     stream = torch.cuda.current_stream(dev)
 
     def step() -> None:
@@ -236,10 +256,8 @@ def run_e2e(args, dev, world: int, rank: int) -> dict:
         col.update("mlp.weight", x_h.to(dev, non_blocking=True))
         rms = col.finalize_on_device()["rms"]["mlp.weight"]
         for i, w in enumerate(w_h):
-            p, s = quantize_mxfp4(w.to(dev, non_blocking=True), scale_percentile=PCT, gamma=rms,
-                                  mse_clip_depth=DEPTH)
-            p_h[i].copy_(p, non_blocking=True)
-            s_h[i].copy_(s, non_blocking=True)
+            streamer.quantize(w, p_h[i], s_h[i], scale_percentile=PCT, gamma=rms, mse_clip_depth=DEPTH)
+        streamer.finish()
 
     for _ in range(max(2, args.warmup)):
         step()
@@ -265,6 +283,78 @@ def run_e2e(args, dev, world: int, rank: int) -> dict:
         "h2d_bytes_per_step": int(elems * 2 + TOKENS * HIDDEN * 2),
         "d2h_bytes_per_step": int(elems // 2 + elems // 32),
         "ms_per_step": round(ms / steps, 3),
+        "path": "ActivationCollector + ChunkStreamer (pinned host in/out, H2D/compute/D2H streams)",
+    }
+
+
+def run_xtx(args, dev, world: int, rank: int) -> dict:
+    """Calibration X^T X: 65536 x 5120 bf16 tokens -> full fp32 Gram on tcgen05.
+
+    Tokens are split across ranks (strong scaling); each rank accumulates its
+    slice, then one NCCL all-reduce sums the 105 MB Gram.  Reported: whole-job
+    tokens/s (max over ranks), and the tensor roofline of the local kernel.
+    """
+    import torch
+
+    from mxwave_b200 import _lib, synthetic
+
+    lib = _lib.load()
+    total_tokens, k = XTX_TOKENS, HIDDEN
+    lo, hi = total_tokens * rank // world, total_tokens * (rank + 1) // world
+    x = synthetic.torch_activations(hi - lo, k, seed=300 + rank, device=dev)
+    gram = torch.zeros(k, k, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(record=None) -> None:
+        gram.zero_()
+        if record is not None:
+            record[0].record(stream)
+        _lib.check(lib.mxw_accumulate_xtx(x.data_ptr(), hi - lo, k, k, gram.data_ptr(), k, None,
+                                          stream.cuda_stream), "xtx")
+        if record is not None:
+            record[1].record(stream)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(gram, op=dist.ReduceOp.SUM)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(args.steps):
+        step(kev[i])
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b)
+    k_ms = sum(e0.elapsed_time(e1) for e0, e1 in kev) / len(kev)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms, k_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, k_ms = float(t[0]), float(t[1])
+    peak = _peaks_tensor()
+    flops = 2.0 * (hi - lo) * k * k
+    achieved = flops / (k_ms * 1e-3) / 1e12
+    return {
+        "metric": "calib tokens/s for X^T X",
+        "value": round(total_tokens * args.steps / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "scaling": "strong",
+        "config": {"workload": f"full X^T X of {total_tokens} x {k} bf16 activations -> fp32 Gram, "
+                               f"tokens split over {world} GPU(s), NCCL all-reduce of the Gram"},
+        "ms_per_step": round(ms / args.steps, 4),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak[0], "unit": "TFLOP/s",
+                     "frac": round(achieved / peak[0], 4), "peak_kind": peak[1], "kernel": "xtx_kernel (tcgen05)",
+                     "flops_per_launch": flops, "avg_launch_ms": round(k_ms, 4)},
+        "gpu_launches": args.steps,
     }
 
 
@@ -365,6 +455,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-xtx", action="store_true", help="skip the X^T X calibration measurement")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per quantize launch from an ncu capture (recorded in the roofline)")
     args = ap.parse_args()

@@ -261,6 +261,50 @@ class ActivationCollector:
     def observation_counts(self) -> dict[str, int]:
         return dict(self._counts)
 
+    def all_reduce(self, group: Any = None, device: torch.device | None = None) -> None:
+        """Sum this collector's accumulators and counts over a process group.
+
+        For token-sharded calibration: every rank accumulates its own tokens,
+        then one all-reduce (a single flat fp32 buffer, plus one int64 buffer
+        of counts) gives every rank the totals.  A target this rank did not
+        observe contributes zeros; a target no rank observed stays unobserved,
+        so finalize() still reports it.
+        """
+        import torch.distributed as dist
+
+        names = sorted(self.target_widths)
+        if device is None:
+            existing = next(iter(self._absolute_sums.values() or self._square_sums.values() or
+                                 self._gram_sums.values()), None)
+            device = existing.device if existing is not None else torch.device("cuda", torch.cuda.current_device())
+        layout: list[tuple[dict[str, torch.Tensor], str, tuple[int, ...]]] = []
+        for name in names:
+            width = self.target_widths[name]
+            if "mean-abs" in self.objectives:
+                layout.append((self._absolute_sums, name, (width,)))
+            if "rms" in self.objectives:
+                layout.append((self._square_sums, name, (width,)))
+            if "block-hessian" in self.objectives:
+                layout.append((self._gram_sums, name, (width // BLOCK_SIZE, BLOCK_SIZE, BLOCK_SIZE)))
+        sizes = [math.prod(shape) for _, _, shape in layout]
+        flat = torch.zeros(sum(sizes), dtype=torch.float32, device=device)
+        offset = 0
+        for (dest, name, _shape), size in zip(layout, sizes):
+            value = dest.get(name)
+            if value is not None:
+                flat[offset : offset + size].copy_(value.reshape(-1))
+            offset += size
+        counts = torch.tensor([self._counts.get(n, 0) for n in names], dtype=torch.int64, device=device)
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+        offset = 0
+        for (dest, name, shape), size in zip(layout, sizes):
+            dest[name] = flat[offset : offset + size].view(shape).clone()
+            offset += size
+        self._counts = {n: int(c) for n, c in zip(names, counts.tolist()) if int(c) > 0}
+        self._last = None
+        self._last_ref = None
+
 
 def attach_activation_hooks(
     model: torch.nn.Module,

@@ -161,6 +161,42 @@ def quantize_mxfp4(
 
 
 @torch.no_grad()
+def quantize_into(
+    weight: torch.Tensor,
+    packed: torch.Tensor,
+    scales: torch.Tensor,
+    *,
+    scale_percentile: float = 99.5,
+    gamma: torch.Tensor | None = None,
+    hessian: torch.Tensor | None = None,
+    method: QuantizationMethod = "mse",
+    mse_clip_depth: int = 1,
+    flags: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """Quantize a 2-D CUDA weight into caller-owned outputs on `stream`.
+
+    The pipeline building block behind the streamer: no validation beyond the
+    C ABI's argument checks and no allocation.  `gamma` / `hessian` must be
+    fp32 CUDA tensors already validated by the caller; `flags` (int32, one
+    element) receives MXW_FLAG_NONFINITE for a NaN/inf input.
+    """
+    rows, cols = weight.shape
+    w, dtype_code = _as_kernel_input(weight)
+    handle = (stream or torch.cuda.current_stream(weight.device)).cuda_stream
+    lib = _lib.load()
+    with torch.cuda.device(weight.device):
+        status = lib.mxw_quantize_mxfp4(
+            w.data_ptr(), dtype_code, rows, cols, w.stride(0), float(scale_percentile),
+            None if gamma is None else gamma.data_ptr(),
+            None if hessian is None else hessian.data_ptr(),
+            _lib.MXW_METHOD_RTN if method == "rtn" else _lib.MXW_METHOD_MSE, mse_clip_depth,
+            packed.data_ptr(), scales.data_ptr(), None if flags is None else flags.data_ptr(), handle,
+        )
+    _lib.check(status, "mxw_quantize_mxfp4")
+
+
+@torch.no_grad()
 def dequant_mxfp4(
     packed: torch.Tensor,
     scales: torch.Tensor,
@@ -239,5 +275,6 @@ __all__ = [
     "QuantizationMethod",
     "compute_block_hessian",
     "dequant_mxfp4",
+    "quantize_into",
     "quantize_mxfp4",
 ]
