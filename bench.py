@@ -185,7 +185,7 @@ def run_ours(args) -> None:
     q_ms = sum(a.elapsed_time(b) for a, b in ev_q) / len(ev_q)
 
     # ---- end to end through the public API, host pinned buffers.
-    e2e = run_e2e(args, dev, world, rank)
+    e2e = None if args.no_e2e else run_e2e(args, dev, world, rank)
     # ---- calibration: X^T X on the tensor cores (config 3's token set).
     xtx = None if args.no_xtx else run_xtx(args, dev, world, rank)
 
@@ -456,6 +456,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-xtx", action="store_true", help="skip the X^T X calibration measurement")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--traffic", type=float, default=None,
                     help="dram bytes per quantize launch from an ncu capture (recorded in the roofline)")
     args = ap.parse_args()

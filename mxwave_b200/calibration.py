@@ -164,8 +164,11 @@ class ActivationCollector:
                 raise ValueError("Token exclusion requires [batch, sequence, channels] inputs")
             if activation.shape[1] <= self.skip_first_tokens:
                 raise ValueError("Token exclusion would remove every observation in a window")
-        same = (self._last is not None and self._last_ref is not None and self._last_ref() is activation
-                and activation._version == self._last_version)
+        # Inference tensors carry no version counter, so an in-place change
+        # between two hooks could not be seen: they are always re-read.
+        version = None if activation.is_inference() else activation._version
+        same = (version is not None and self._last is not None and self._last_ref is not None
+                and self._last_ref() is activation and version == self._last_version)
         if same:
             count, d_abs, d_sq, d_gram = self._last
             self.reduced_reads += 1
@@ -173,7 +176,7 @@ class ActivationCollector:
             count, d_abs, d_sq, d_gram = self._reduce(activation.detach(), width)
             self._last = (count, d_abs, d_sq, d_gram)
             self._last_ref = weakref.ref(activation)
-            self._last_version = activation._version
+            self._last_version = version
         if count == 0:
             return
         self._counts[target_name] = self._counts.get(target_name, 0) + count

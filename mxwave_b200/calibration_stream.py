@@ -10,6 +10,8 @@ Same signature, validation and result type as the reference
   with asynchronous copies;
 * statistics are accumulated by ``mxwave_b200.calibration.ActivationCollector``
   (sm_100a kernel, one read per distinct input: q/k/v and gate/up share one);
+  layers run under ``torch.no_grad`` rather than inference mode so that the
+  shared inputs keep the version counter that proves them unchanged;
 * with ``process_group`` set, sequences are split across ranks (contiguous,
   equal slices) and each layer's fp32 accumulators and counts are summed with
   one all-reduce before finalisation, so every rank returns the statistics of
@@ -114,7 +116,7 @@ def calibrate_decoder_sequentially(
         )
 
     hidden = new_hidden()
-    with torch.inference_mode():
+    with torch.no_grad():
         for start in range(0, n_local, batch_size):
             rows = local[start : start + batch_size]
             input_ids = torch.tensor(rows, dtype=torch.long, device=device)
@@ -131,7 +133,7 @@ def calibrate_decoder_sequentially(
     counts: dict[str, int] = {}
     next_hidden = new_hidden()
 
-    with torch.inference_mode():
+    with torch.no_grad():
         for layer_index in range(layout.layer_count):
             layer_prefix = f"{layout.stack_prefix}.{layer_index}"
             layer = ref._load_module_from_checkpoint(
