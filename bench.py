@@ -42,6 +42,12 @@ WORKLOAD = (
     f"(rms from {TOKENS}x{HIDDEN} bf16 activations), pct {PCT}, depth {DEPTH}"
 )
 METRIC = "bf16 weight GB/s quantized"
+# dram__bytes_read.sum + dram__bytes_write.sum of one quantize launch of this
+# workload, from the ncu capture summarised in
+# profiles/quantize_tma_kernel_gamma_d1_17408x5120.txt (178.33 MB + 26.55 MB).
+QUANT_TRAFFIC_BYTES = 178_330_112 + 26_546_432
+# The same for one X^T X launch (profiles/xtx_kernel_full_gram_65536x5120.txt).
+XTX_TRAFFIC_BYTES = 4_782_156_000 + 110_097_920
 
 
 def _peaks() -> tuple[float, str]:
@@ -219,7 +225,8 @@ def run_ours(args) -> None:
                    "parallelism": f"tensor-sharded x{world}, no collective"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
-                     "traffic": args.traffic, "kernel": "quantize_tma_kernel<bf16,gamma,top2>",
+                     "traffic": args.traffic, "traffic_unit": "bytes per launch (ncu)",
+                     "kernel": "quantize_tma_kernel<bf16,gamma,top2>",
                      "bytes_per_launch": int(bytes_per_launch), "avg_launch_ms": round(q_ms, 4)},
         "e2e": e2e,
         "cpu_baseline": cpu,
@@ -353,6 +360,7 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
         "ms_per_step": round(ms / args.steps, 4),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak[0], "unit": "TFLOP/s",
                      "frac": round(achieved / peak[0], 4), "peak_kind": peak[1], "kernel": "xtx_kernel (tcgen05)",
+                     "traffic": XTX_TRAFFIC_BYTES if world == 1 else None, "traffic_unit": "bytes per launch (ncu)",
                      "flops_per_launch": flops, "avg_launch_ms": round(k_ms, 4)},
         "gpu_launches": args.steps,
     }
@@ -457,7 +465,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-xtx", action="store_true", help="skip the X^T X calibration measurement")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
-    ap.add_argument("--traffic", type=float, default=None,
+    ap.add_argument("--traffic", type=float, default=QUANT_TRAFFIC_BYTES,
                     help="dram bytes per quantize launch from an ncu capture (recorded in the roofline)")
     args = ap.parse_args()
     if args.warmup < 3:
