@@ -10,6 +10,7 @@ the reference's CPU fp32 implementation.
 from __future__ import annotations
 
 import math
+import weakref
 from typing import Literal
 
 import torch
@@ -55,18 +56,25 @@ class _ValidatedCache:
     """
 
     def __init__(self) -> None:
-        self._seen: dict[int, tuple[int, int, tuple[int, ...]]] = {}
+        # id -> (weak reference, key): the weak reference proves the entry is
+        # about this very object, not a later one that reuses its id.
+        self._seen: dict[int, tuple[weakref.ref, tuple[int, int, tuple[int, ...]]]] = {}
 
     def key(self, t: torch.Tensor) -> tuple[int, int, tuple[int, ...]]:
         return (t.data_ptr(), t._version, tuple(t.shape))
 
     def ok(self, t: torch.Tensor) -> bool:
-        return self._seen.get(id(t)) == self.key(t)
+        if t.is_inference():  # no version counter: an in-place change would go unseen
+            return False
+        entry = self._seen.get(id(t))
+        return entry is not None and entry[0]() is t and entry[1] == self.key(t)
 
     def add(self, t: torch.Tensor) -> None:
+        if t.is_inference():
+            return
         if len(self._seen) > 256:
             self._seen.clear()
-        self._seen[id(t)] = self.key(t)
+        self._seen[id(t)] = (weakref.ref(t), self.key(t))
 
 
 _gamma_ok = _ValidatedCache()

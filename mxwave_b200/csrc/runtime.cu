@@ -33,8 +33,14 @@ int num_sms() {
 }
 
 int set_max_smem(const void* kernel, size_t bytes) {
-  const cudaError_t err =
+  cudaError_t err =
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (err != cudaSuccess) return record_cuda_error(err);
+  // Ask for the whole unified L1/shared array as shared memory: these kernels
+  // stage through shared memory (TMA) and barely use L1, and the default
+  // carveout can leave room for only one CTA per SM.
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             static_cast<int>(cudaSharedmemCarveoutMaxShared));
   return err == cudaSuccess ? MXW_OK : record_cuda_error(err);
 }
 

@@ -3,12 +3,15 @@
 //
 // Replaces ActivationCollector.update (mxwave/calibration.py:206-236): the
 // reference casts x to fp32 and forms values.abs().sum(0), values.square()
-// .sum(0) and einsum("nbi,nbj->bij") per hooked call.  Here each CTA owns one
-// 32-channel strip (= one MXFP4 block column) for all tokens, streams it
-// through shared memory with TMA, keeps fp32 partial sums per 256-token tile
-// and folds them into fp64 accumulators, then adds the strip's totals into
+// .sum(0) and einsum("nbi,nbj->bij") per hooked call.  Here a thread-block
+// cluster owns one 32-channel strip (= one MXFP4 block column); each CTA of
+// the cluster streams one contiguous token slice of the strip through shared
+// memory with TMA, keeps fp32 partial sums per 256-token tile and folds them
+// into fp64 accumulators.  CTA rank 0 then reads every rank's partials over
+// distributed shared memory in rank order and adds the strip's totals into
 // the caller's fp32 buffers.  Every output element is written by exactly one
-// CTA in a fixed order, so the result is deterministic run to run.
+// CTA with a fixed summation order, so the result is deterministic run to
+// run, and no global scratch memory is needed.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -16,6 +19,10 @@
 #include "common.cuh"
 #include "runtime.h"
 #include "tma.cuh"
+
+#include <cooperative_groups.h>
+
+namespace cg = cooperative_groups;
 
 namespace mxw {
 
@@ -37,6 +44,16 @@ __device__ __forceinline__ float load_elem(const uint8_t* row, int c) {
   return reinterpret_cast<const float*>(row)[c];
 }
 
+// Shared-memory doubles per CTA: the reduction buffer (per thread) and this
+// CTA's partials; the moments-only kernel needs far less, so more CTAs fit.
+template <bool GRAM>
+struct StatSmem {
+  static constexpr int kRed = GRAM ? 16 : 4;
+  static constexpr int kRes = 1 + 64 + (GRAM ? 1024 : 0);
+  static constexpr size_t kBytes = 128 + kStatStages * kStatTileBytes + 2 * kStatStages * sizeof(uint64_t) +
+                                   (256 * kRed + kRes) * sizeof(double);
+};
+
 struct StatParams {
   int64_t tokens, cols, n_tiles;
   float* sum_abs;
@@ -46,20 +63,26 @@ struct StatParams {
 };
 
 template <int DT, bool MOMENTS, bool GRAM>
-__global__ void __launch_bounds__(kStatThreads, 1)
+__global__ void __launch_bounds__(kStatThreads, GRAM ? 2 : 3)
     activation_stats_kernel(const __grid_constant__ CUtensorMap map, const StatParams P) {
   constexpr int TR = StatElem<DT>::kTileRows;
   constexpr int RB = 32 * StatElem<DT>::kBytes;  // bytes per tile row
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Unswizzled TMA tiles need 128-byte aligned destinations.
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStatStages * kStatTileBytes);
   uint64_t* empty = full + kStatStages;
-  double* red = reinterpret_cast<double*>(empty + kStatStages);  // [256][16] doubles for the final reduction
+  double* red = reinterpret_cast<double*>(empty + kStatStages);  // [256][16 or 4] doubles: the CTA reduction
+  double* res = red + 256 * StatSmem<GRAM>::kRed;  // failure flag, 64 moment and 1024 Gram partials of this CTA
 
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned rank = cluster.block_rank();  // this CTA's token slice of the strip
+  const unsigned nrank = cluster.num_blocks();
   __shared__ int s_fail;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t col0 = static_cast<int64_t>(blockIdx.x) * 32;
+  const int64_t i_begin = P.n_tiles * rank / nrank, i_end = P.n_tiles * (rank + 1) / nrank;
   if (threadIdx.x == 0) {
     s_fail = 0;
     for (int s = 0; s < kStatStages; ++s) {
@@ -70,14 +93,15 @@ __global__ void __launch_bounds__(kStatThreads, 1)
   }
   __syncthreads();
 
+  const int t = threadIdx.x;  // consumers: 0..255
   if (warp == kStatConsumers) {
     if (lane == 0) {
       prefetch_tensormap(&map);
       bool ok = true;
-      int64_t i = 0;
-      for (; i < P.n_tiles; ++i) {
-        const int s = static_cast<int>(i % kStatStages);
-        if (i >= kStatStages && !mbar_wait(&empty[s], static_cast<uint32_t>((i / kStatStages - 1) & 1))) {
+      int64_t n = 0;
+      for (int64_t i = i_begin; i < i_end; ++i, ++n) {
+        const int s = static_cast<int>(n % kStatStages);
+        if (n >= kStatStages && !mbar_wait(&empty[s], static_cast<uint32_t>((n / kStatStages - 1) & 1))) {
           ok = false;
           break;
         }
@@ -85,124 +109,148 @@ __global__ void __launch_bounds__(kStatThreads, 1)
         tma_load_2d(stages + s * kStatTileBytes, &map, &full[s], static_cast<int32_t>(col0),
                     static_cast<int32_t>(i * TR));
       }
-      for (int64_t j = (i > kStatStages ? i - kStatStages : 0); j < i; ++j)
+      // Never leave copies in flight: wait for the last issued stages.
+      for (int64_t j = (n > kStatStages ? n - kStatStages : 0); j < n; ++j)
         if (!mbar_wait(&full[j % kStatStages], static_cast<uint32_t>((j / kStatStages) & 1))) ok = false;
-      if (!ok && P.flags) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
+      if (!ok) atomicOr(&s_fail, 1);
     }
-    return;
-  }
-
-  const int t = threadIdx.x;  // 0..255
-  // Moments: channel pair p (columns 2p, 2p+1), token residue g (16 groups).
-  const int mp = t & 15, mg = t >> 4;
-  double macc_abs[2] = {0.0, 0.0}, macc_sq[2] = {0.0, 0.0};
-  // Gram: 4x4 sub-block (i0, j0) of the 32x32 block, token residue gg (4 groups).
-  const int gi0 = 4 * ((t & 63) >> 3), gj0 = 4 * (t & 7), gg = t >> 6;
-  double gacc[16];
+  } else {
+    // Moments: channel pair p (columns 2p, 2p+1), token residue g (16 groups).
+    const int mp = t & 15, mg = t >> 4;
+    double macc_abs[2] = {0.0, 0.0}, macc_sq[2] = {0.0, 0.0};
+    // Gram: 4x4 sub-block (i0, j0) of the 32x32 block, token residue gg (4 groups).
+    const int gi0 = 4 * ((t & 63) >> 3), gj0 = 4 * (t & 7), gg = t >> 6;
+    double gacc[16];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) gacc[k] = 0.0;
+    for (int k = 0; k < 16; ++k) gacc[k] = 0.0;
 
-  bool ok = true;
-  for (int64_t i = 0; i < P.n_tiles; ++i) {
-    const int s = static_cast<int>(i % kStatStages);
-    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>((i / kStatStages) & 1)))) {
-      ok = false;
-      break;
-    }
-    const uint8_t* tile = stages + s * kStatTileBytes;
-    const int64_t remaining = P.tokens - i * TR;
-    const int valid = remaining < TR ? static_cast<int>(remaining) : TR;  // rows past the end are TMA zero-fill
-    if constexpr (MOMENTS) {
-      float a0 = 0.f, a1 = 0.f, q0 = 0.f, q1 = 0.f;
-      for (int r = mg; r < valid; r += 16) {
-        const float x0 = load_elem<DT>(tile + r * RB, 2 * mp), x1 = load_elem<DT>(tile + r * RB, 2 * mp + 1);
-        a0 = __fadd_rn(a0, fabsf(x0));
-        a1 = __fadd_rn(a1, fabsf(x1));
-        q0 = __fmaf_rn(x0, x0, q0);
-        q1 = __fmaf_rn(x1, x1, q1);
+    bool ok = true;
+    int64_t n = 0;
+    for (int64_t i = i_begin; i < i_end; ++i, ++n) {
+      const int s = static_cast<int>(n % kStatStages);
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>((n / kStatStages) & 1)))) {
+        ok = false;
+        break;
       }
-      macc_abs[0] += a0;
-      macc_abs[1] += a1;
-      macc_sq[0] += q0;
-      macc_sq[1] += q1;
-    }
-    if constexpr (GRAM) {
-      float acc[16];
+      const uint8_t* tile = stages + s * kStatTileBytes;
+      const int64_t remaining = P.tokens - i * TR;
+      const int valid = remaining < TR ? static_cast<int>(remaining) : TR;  // rows past the end are TMA zero-fill
+      if constexpr (MOMENTS) {
+        float a0 = 0.f, a1 = 0.f, q0 = 0.f, q1 = 0.f;
+        for (int r = mg; r < valid; r += 16) {
+          const float x0 = load_elem<DT>(tile + r * RB, 2 * mp), x1 = load_elem<DT>(tile + r * RB, 2 * mp + 1);
+          a0 = __fadd_rn(a0, fabsf(x0));
+          a1 = __fadd_rn(a1, fabsf(x1));
+          q0 = __fmaf_rn(x0, x0, q0);
+          q1 = __fmaf_rn(x1, x1, q1);
+        }
+        macc_abs[0] += a0;
+        macc_abs[1] += a1;
+        macc_sq[0] += q0;
+        macc_sq[1] += q1;
+      }
+      if constexpr (GRAM) {
+        float acc[16];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) acc[k] = 0.f;
-      for (int r = gg; r < valid; r += 4) {
-        const uint8_t* row = tile + r * RB;
-        float xi[4], xj[4];
+        for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+        for (int r = gg; r < valid; r += 4) {
+          const uint8_t* row = tile + r * RB;
+          float xi[4], xj[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          xi[k] = load_elem<DT>(row, gi0 + k);
-          xj[k] = load_elem<DT>(row, gj0 + k);
+          for (int k = 0; k < 4; ++k) {
+            xi[k] = load_elem<DT>(row, gi0 + k);
+            xj[k] = load_elem<DT>(row, gj0 + k);
+          }
+#pragma unroll
+          for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc[a * 4 + b] = __fmaf_rn(xi[a], xj[b], acc[a * 4 + b]);
         }
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int b = 0; b < 4; ++b) acc[a * 4 + b] = __fmaf_rn(xi[a], xj[b], acc[a * 4 + b]);
+        for (int k = 0; k < 16; ++k) gacc[k] += acc[k];
       }
-#pragma unroll
-      for (int k = 0; k < 16; ++k) gacc[k] += acc[k];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-  }
-  // Every consumer warp leaves the loop (all waits are bounded); agree on the
-  // verdict before any write-back so a timed-out CTA writes nothing.
-  if (!ok && lane == 0) atomicOr(&s_fail, 1);
-  asm volatile("bar.sync 1, 256;" ::: "memory");
-  if (s_fail) {
-    if (P.flags && t == 0) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
-    return;
-  }
+    if (!ok && lane == 0) atomicOr(&s_fail, 1);
 
-  // Fixed-order reductions across the token residues, then one add into the
-  // caller's fp32 accumulators (these CTAs own their columns exclusively).
-  // Named barrier 1 synchronises the 256 consumer threads only.
-  if constexpr (MOMENTS) {
-    red[t * 4 + 0] = macc_abs[0];
-    red[t * 4 + 1] = macc_abs[1];
-    red[t * 4 + 2] = macc_sq[0];
-    red[t * 4 + 3] = macc_sq[1];
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (t < 16) {
-      double sa0 = 0, sa1 = 0, sq0 = 0, sq1 = 0;
-      for (int g = 0; g < 16; ++g) {
-        const double* v = red + (g * 16 + t) * 4;
-        sa0 += v[0];
-        sa1 += v[1];
-        sq0 += v[2];
-        sq1 += v[3];
+    // Fixed-order reductions across the token residues into this CTA's
+    // partials `res` (named barrier 1: the 256 consumer threads only).
+    if constexpr (MOMENTS) {
+      red[t * 4 + 0] = macc_abs[0];
+      red[t * 4 + 1] = macc_abs[1];
+      red[t * 4 + 2] = macc_sq[0];
+      red[t * 4 + 3] = macc_sq[1];
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (t < 16) {
+        double v[4] = {0.0, 0.0, 0.0, 0.0};
+        for (int g = 0; g < 16; ++g)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) v[k] += red[(g * 16 + t) * 4 + k];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) res[1 + t * 4 + k] = v[k];
       }
-      const int64_t c = col0 + 2 * t;
-      if (P.sum_abs) {
-        if (c < P.cols) P.sum_abs[c] += static_cast<float>(sa0);
-        if (c + 1 < P.cols) P.sum_abs[c + 1] += static_cast<float>(sa1);
-      }
-      if (P.sum_sq) {
-        if (c < P.cols) P.sum_sq[c] += static_cast<float>(sq0);
-        if (c + 1 < P.cols) P.sum_sq[c + 1] += static_cast<float>(sq1);
-      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
     }
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-  }
-  if constexpr (GRAM) {
+    if constexpr (GRAM) {
 #pragma unroll
-    for (int k = 0; k < 16; ++k) red[t * 16 + k] = gacc[k];
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (t < 64) {
-      float* G = P.gram_blocks + blockIdx.x * 1024;
+      for (int k = 0; k < 16; ++k) red[t * 16 + k] = gacc[k];
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (t < 64) {
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        double v = 0.0;
-        for (int g = 0; g < 4; ++g) v += red[(g * 64 + t) * 16 + k];
-        const int a = k >> 2, b = k & 3;
-        G[(gi0 + a) * 32 + gj0 + b] += static_cast<float>(v);
+        for (int k = 0; k < 16; ++k) {
+          double v = 0.0;
+          for (int g = 0; g < 4; ++g) v += red[(g * 64 + t) * 16 + k];
+          res[65 + t * 16 + k] = v;
+        }
       }
     }
   }
+  __syncthreads();
+  if (threadIdx.x == 0) res[0] = s_fail ? 1.0 : 0.0;
+
+  // Every thread of every CTA of the cluster reaches both cluster barriers
+  // exactly once (every wait above is bounded), so neither waits forever.
+  cluster_sync_all();
+  if (rank == 0 && warp < kStatConsumers) {
+    // The strip's totals in rank order 0..nrank-1 (a fixed order: the result is
+    // deterministic).  A failed slice anywhere leaves the outputs untouched.
+    bool failed = false;
+    for (unsigned r = 0; r < nrank; ++r) failed |= cluster.map_shared_rank(res, r)[0] != 0.0;
+    if (failed) {
+      if (P.flags && t == 0) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
+    } else {
+      if (MOMENTS && t < 16) {
+        double v[4] = {0.0, 0.0, 0.0, 0.0};
+        for (unsigned r = 0; r < nrank; ++r) {
+          const double* rr = cluster.map_shared_rank(res, r);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) v[k] += rr[1 + t * 4 + k];
+        }
+        const int64_t c = col0 + 2 * t;
+        if (P.sum_abs) {
+          if (c < P.cols) P.sum_abs[c] += static_cast<float>(v[0]);
+          if (c + 1 < P.cols) P.sum_abs[c + 1] += static_cast<float>(v[1]);
+        }
+        if (P.sum_sq) {
+          if (c < P.cols) P.sum_sq[c] += static_cast<float>(v[2]);
+          if (c + 1 < P.cols) P.sum_sq[c + 1] += static_cast<float>(v[3]);
+        }
+      }
+      if (GRAM && t < 64) {
+        const int gi0 = 4 * ((t & 63) >> 3), gj0 = 4 * (t & 7);
+        float* G = P.gram_blocks + blockIdx.x * 1024;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          double v = 0.0;
+          for (unsigned r = 0; r < nrank; ++r) v += cluster.map_shared_rank(res, r)[65 + t * 16 + k];
+          G[(gi0 + (k >> 2)) * 32 + gj0 + (k & 3)] += static_cast<float>(v);
+        }
+      }
+    }
+  }
+  // Keep every CTA's shared memory alive until rank 0 has read it.
+  cluster_sync_all();
 }
 
 // Plain-load fallback (unaligned base or row stride): one thread per channel
@@ -236,11 +284,21 @@ __global__ void stats_plain_kernel(const void* __restrict__ x, int64_t ld, StatP
   }
 }
 
+// Token slices per strip (the cluster size): up to 4, keeping at least 8
+// tiles per slice.  Measured on B200 at 5120 channels: 8192 tokens take
+// 31 us with 4 slices against 39 us with 1 or 8 (one slice leaves too few
+// loads in flight per SM; 8 short slices pay the per-CTA set-up and the two
+// cluster barriers more often than they gain).
+static int stat_slices(int64_t tiles) {
+  int S = 1;
+  while (S < 4 && tiles >= 8 * (2 * S)) S *= 2;
+  return S;
+}
+
 template <int DT, bool M, bool G>
 static int launch_stats_tma(const void* x, int64_t ld, const StatParams& P, cudaStream_t stream) {
   constexpr int TR = StatElem<DT>::kTileRows;
-  const size_t smem = 1024 + kStatStages * kStatTileBytes + 2 * kStatStages * sizeof(uint64_t) +
-                      256 * 16 * sizeof(double);
+  const size_t smem = StatSmem<G>::kBytes;
   CUtensorMap map;
   const CUtensorMapDataType dt = DT == MXW_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : DT == MXW_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -253,7 +311,25 @@ static int launch_stats_tma(const void* x, int64_t ld, const StatParams& P, cuda
   if (rc != MXW_OK) return rc;
   StatParams Q = P;
   Q.n_tiles = (P.tokens + TR - 1) / TR;
-  kern<<<static_cast<unsigned>((P.cols + 31) / 32), kStatThreads, smem, stream>>>(map, Q);
+  const int64_t strips = (P.cols + 31) / 32;
+  const int S = stat_slices(Q.n_tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(strips), static_cast<unsigned>(S), 1);
+  cfg.blockDim = dim3(kStatThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(S);
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, map, Q);
+  if (err != cudaSuccess) {
+    record_cuda_error(err);
+    return MXW_ECUDA;
+  }
   return check_launch();
 }
 

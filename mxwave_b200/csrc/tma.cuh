@@ -98,4 +98,10 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 
 __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; }
 
+// Cluster-wide barrier (release/acquire), non-aligned form: every thread of
+// every CTA in the cluster must execute it the same number of times.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
 }  // namespace mxw

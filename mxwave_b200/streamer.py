@@ -21,7 +21,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from .core import BLOCK_SIZE, quantize_into
+from .core import BLOCK_SIZE, _gamma_ok, _hessian_ok, quantize_into
 
 
 @dataclass
@@ -115,16 +115,27 @@ class ChunkStreamer:
             scales_out = torch.empty((rows, cols // BLOCK_SIZE), dtype=torch.uint8, pin_memory=True)
         g = h = None
         with torch.cuda.device(self.device):
+            # Validated once per unchanged statistic tensor (a host sync each
+            # time otherwise, which would serialise the copy pipeline).
             if gamma is not None:
+                if gamma.shape != (cols,):
+                    raise ValueError(f"gamma must have shape {(cols,)}, got {tuple(gamma.shape)}")
+                if not _gamma_ok.ok(gamma):
+                    if not torch.isfinite(gamma).all() or (gamma < 0).any():
+                        raise ValueError("gamma must contain finite, non-negative magnitudes")
+                    _gamma_ok.add(gamma)
                 g = gamma.to(device=self.device, dtype=torch.float32).contiguous()
-                if g.shape != (cols,) or not torch.isfinite(g).all() or (g < 0).any():
-                    raise ValueError("gamma must contain finite, non-negative magnitudes")
             if hessian is not None:
+                if hessian.shape != (cols // BLOCK_SIZE, BLOCK_SIZE, BLOCK_SIZE):
+                    raise ValueError(
+                        f"hessian must have shape {(cols // BLOCK_SIZE, BLOCK_SIZE, BLOCK_SIZE)}, "
+                        f"got {tuple(hessian.shape)}"
+                    )
+                if not _hessian_ok.ok(hessian):
+                    if not torch.isfinite(hessian).all():
+                        raise ValueError("hessian contains NaN or infinity")
+                    _hessian_ok.add(hessian)
                 h = hessian.to(device=self.device, dtype=torch.float32).contiguous()
-                if h.shape != (cols // BLOCK_SIZE, BLOCK_SIZE, BLOCK_SIZE):
-                    raise ValueError(f"hessian must have shape {(cols // BLOCK_SIZE, BLOCK_SIZE, BLOCK_SIZE)}")
-                if not torch.isfinite(h).all():
-                    raise ValueError("hessian contains NaN or infinity")
             slab_rows = max(1, min(rows, self.slab_bytes // max(1, cols * weight.element_size())))
             self._ensure(slab_rows, cols, weight.dtype)
             flags = [self._next_flag_for(name, start, min(start + slab_rows, rows)) for start in range(0, rows, slab_rows)]

@@ -159,3 +159,22 @@ def test_xtx_accumulates_with_strides(cuda_device) -> None:
     ref = oracle.gram(xf[:, :512]) + np.eye(512)
     assert _full_err(g[:, :512].cpu().numpy().astype(np.float64), ref) < RTOL
     assert float(g[:, 512:].abs().max()) == 0.0  # padding columns untouched
+
+
+@pytest.mark.parametrize("tokens", [300, 4097, 8192, 65536])
+def test_statistics_are_deterministic_run_to_run(tokens, cuda_device) -> None:
+    """The strip totals are folded in a fixed order: two runs give identical bits."""
+    lib = _lib.load()
+    x, _ = _x(tokens, 640, 11, cuda_device, torch.bfloat16)
+    outs = []
+    for _ in range(2):
+        s1 = torch.zeros(640, device=cuda_device)
+        s2 = torch.zeros(640, device=cuda_device)
+        g = torch.zeros(20, 32, 32, device=cuda_device)
+        st = lib.mxw_accumulate_activation_stats(x.data_ptr(), _lib.MXW_BF16, tokens, 640, 640, s1.data_ptr(),
+                                                 s2.data_ptr(), g.data_ptr(), None, _stream(cuda_device))
+        assert st == _lib.MXW_OK
+        outs.append((s1, s2, g))
+    torch.cuda.synchronize()
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
