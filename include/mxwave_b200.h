@@ -18,6 +18,7 @@
 #ifndef MXWAVE_B200_H_
 #define MXWAVE_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -88,6 +89,31 @@ MXW_API int mxw_quantize_mxfp4(const void* weight, int dtype, int64_t rows, int6
  */
 MXW_API int mxw_dequant_mxfp4(const uint8_t* packed, const uint8_t* scales, int64_t rows, int64_t cols,
                       float* out, void* stream);
+
+/*
+ * Quantization-error sums for the SQNR family: one pass over an original
+ * matrix [rows, cols] (row stride ld, dtype MXW_BF16/F16/F32) and its
+ * reconstruction -- either a dense matrix (`reconstructed`, dtype rdtype, row
+ * stride rld) or the packed MXFP4 bytes and E8M0 scales decoded on the fly
+ * (packed/scales, cols % 32 == 0); exactly one of the two.  Writes
+ *   sums[0] = sum o^2, sums[1] = sum (o - r)^2,
+ *   sums[2], sums[3] = the same weighted by gamma^2 per input channel
+ *   (gamma[cols]) or by the 32x32 block quadratic form (hessian[cols/32][32][32]),
+ *   else 0.
+ * fp64 accumulation with a fixed reduction order (bit-reproducible).
+ * `workspace`: device memory of at least mxw_error_sums_workspace_size(rows,
+ * cols) bytes, 16-byte aligned, whose first 16 bytes are zero before the first
+ * call on it (each call leaves them zero again).  Calls sharing a workspace
+ * must not overlap on the device.
+ * Replaces the reductions of sqnr / channel_weighted_sqnr /
+ * block_hessian_weighted_sqnr (mxwave/verify.py:24-86) and, with packed input,
+ * the dequant_mxfp4 they follow in the engines (mxwave/engine.py:439-458).
+ */
+MXW_API size_t mxw_error_sums_workspace_size(int64_t rows, int64_t cols);
+MXW_API int mxw_error_sums(const void* original, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                           const void* reconstructed, int rdtype, int64_t rld, const uint8_t* packed,
+                           const uint8_t* scales, const float* gamma, const float* hessian, double* sums,
+                           void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Per-channel moments of activations x [tokens, cols] (row stride ld), added

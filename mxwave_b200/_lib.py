@@ -52,6 +52,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mxw_accumulate_xtx": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "mxw_finalize_moments": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _vp]),
     "mxw_finalize_block_hessian": (_int, [_vp, _int, _i64, _i64, _i64, ctypes.c_double, _int, _vp, _vp]),
+    "mxw_error_sums_workspace_size": (ctypes.c_size_t, [_i64, _i64]),
+    "mxw_error_sums": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+                              ctypes.c_size_t, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None

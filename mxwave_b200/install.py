@@ -20,6 +20,9 @@ mxwave.calibration.attach_activation_hooks
   calibration_stream.py:385-404        mxwave_b200.calibration.attach_activation_hooks
 mxwave.calibration_stream.calibrate_decoder_sequentially
   calibration_cli.py                   mxwave_b200.calibration_stream.calibrate_decoder_sequentially
+mxwave.verify.sqnr / channel_weighted_sqnr / block_hessian_weighted_sqnr
+  engine.py:447-458,565-585            mxwave_b200.verify (same names)
+  expert_engine.py:620,776
 =====================================  ============================================
 
 The engines keep their planning, durability, manifests and CLI; only the
@@ -49,7 +52,7 @@ class Installation:
 
 
 def _replacements() -> dict[str, dict[str, Any]]:
-    from . import calibration, calibration_stream, checkpoint, core
+    from . import calibration, calibration_stream, checkpoint, core, verify
 
     return {
         "mxwave.core": {
@@ -62,11 +65,20 @@ def _replacements() -> dict[str, dict[str, Any]]:
             "dequant_mxfp4": core.dequant_mxfp4,
             "iter_quantized_row_chunks": checkpoint.iter_quantized_row_chunks,
             "read_tensor_row_range": checkpoint.read_tensor_row_range,
+            "sqnr": verify.sqnr,
+            "channel_weighted_sqnr": verify.channel_weighted_sqnr,
+            "block_hessian_weighted_sqnr": verify.block_hessian_weighted_sqnr,
         },
         "mxwave.expert_engine": {
             "quantize_mxfp4": core.quantize_mxfp4,
             "dequant_mxfp4": core.dequant_mxfp4,
             "iter_quantized_row_chunks": checkpoint.iter_quantized_row_chunks,
+            "sqnr": verify.sqnr,
+        },
+        "mxwave.verify": {
+            "sqnr": verify.sqnr,
+            "channel_weighted_sqnr": verify.channel_weighted_sqnr,
+            "block_hessian_weighted_sqnr": verify.block_hessian_weighted_sqnr,
         },
         "mxwave.checkpoint": {"iter_quantized_row_chunks": checkpoint.iter_quantized_row_chunks},
         "mxwave.shard": {"read_tensor_row_range": checkpoint.read_tensor_row_range},

@@ -153,3 +153,37 @@ def finalize_block_hessian(block_sums: np.ndarray, count: int, damp: float, mode
     else:
         h[..., idx, idx] += h[..., idx, idx].mean(axis=-1, keepdims=True) * damp
     return h
+
+
+def error_sums(
+    original: np.ndarray,
+    reconstructed: np.ndarray,
+    gamma: np.ndarray | None = None,
+    hessian: np.ndarray | None = None,
+) -> np.ndarray:
+    """float64 sums behind the SQNR family, verify.py:24-86.
+
+    [sum o^2, sum (o - r)^2, weighted signal, weighted noise]; the difference
+    o - r is formed in fp32 as the reference forms it, the rest in float64.
+    Weighted: gamma^2 per input channel, or the 32x32 block quadratic form.
+    """
+    o32 = np.asarray(original, dtype=np.float32)
+    d32 = (o32 - np.asarray(reconstructed, dtype=np.float32)).astype(np.float32)
+    o, d = o32.astype(np.float64), d32.astype(np.float64)
+    out = np.zeros(4)
+    out[0], out[1] = (o * o).sum(), (d * d).sum()
+    if gamma is not None:
+        g2 = np.asarray(gamma, dtype=np.float64) ** 2
+        out[2], out[3] = (o * o * g2).sum(), (d * d * g2).sum()
+    elif hessian is not None:
+        h = np.asarray(hessian, dtype=np.float64)
+        ob, db = o.reshape(o.shape[0], -1, 32), d.reshape(d.shape[0], -1, 32)
+        out[2] = np.einsum("rbi,bij,rbj->", ob, h, ob)
+        out[3] = np.einsum("rbi,bij,rbj->", db, h, db)
+    return out
+
+
+def sqnr_db(signal: float, noise: float) -> float:
+    """10 log10(signal / noise) with both clamped below at fp32(1e-12), as verify.py does."""
+    floor = float(np.float32(1e-12))
+    return float(10.0 * np.log10(max(signal, floor) / max(noise, floor)))
