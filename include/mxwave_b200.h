@@ -116,6 +116,31 @@ MXW_API int mxw_error_sums(const void* original, int dtype, int64_t rows, int64_
                            void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * mxw_error_sums without a workspace, for callers that cannot allocate device
+ * memory when they call: processes that reserve their whole device memory
+ * budget at start-up and forbid later allocations (a serving process that has
+ * carved up HBM, or a host application whose own pool owns every device
+ * byte), and health checks that must still run when the device is out of
+ * memory.  No counterpart in the reference.
+ * Same arguments and results as mxw_error_sums minus the workspace.  Its
+ * scratch is a fixed 65,552-byte device array in this library (a 16-byte
+ * ticket plus fp64 partials for up to 2048 CTAs, i.e. 8 per SM on GPUs of up
+ * to 256 SMs), held by every GPU that loads the library until the process
+ * exits.  A launch that would need more scratch returns MXW_EUNSUPPORTED (use
+ * mxw_error_sums with a workspace instead).  The call allocates nothing: it
+ * clears the ticket with an asynchronous memset on `stream`, then launches.
+ * The first call on a device looks up the array's device address (and may
+ * load this library's kernels onto that device): make that first call before
+ * any stream capture.  All calls share the one array, so calls that overlap
+ * on the device (other streams, other host threads) race and must not be
+ * issued concurrently.
+ */
+MXW_API int mxw_error_sums_noalloc(const void* original, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                   const void* reconstructed, int rdtype, int64_t rld, const uint8_t* packed,
+                                   const uint8_t* scales, const float* gamma, const float* hessian, double* sums,
+                                   void* stream);
+
+/*
  * Per-channel moments of activations x [tokens, cols] (row stride ld), added
  * into sum_abs[cols] (sum |x|) and sum_sq[cols] (sum x^2); either may be NULL.
  * Replaces the mean-abs / rms accumulation of ActivationCollector.update

@@ -20,6 +20,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -234,4 +236,74 @@ extern "C" int mxw_error_sums(const void* original, int dtype, int64_t rows, int
     default:
       return launch_err_rt<MXW_F32>(rt, P, w, s, ctas);
   }
+}
+
+// ------------------------------------------------ no-allocation variant
+//
+// mxw_error_sums_noalloc: the same sums for callers that cannot allocate
+// device memory at call time -- processes that reserve their whole device
+// memory budget up front and forbid later allocations (a serving process
+// that has carved up HBM at start-up, or a host application whose own pool
+// owns every device byte), and health checks that must still run when the
+// device is out of memory.  Its scratch (the CTA ticket and the per-CTA
+// partials) lives in the fixed array below, which every GPU that loads this
+// library holds until the process exits.
+
+namespace mxw {
+
+constexpr int kNoAllocMaxCtas = 2048;  // 8 CTAs per SM on GPUs of up to 256 SMs
+constexpr size_t kNoAllocScratchBytes = 16 + static_cast<size_t>(kNoAllocMaxCtas) * 4 * sizeof(double);  // 65,552
+
+static __device__ __align__(256) unsigned char g_error_sums_scratch[kNoAllocScratchBytes];
+
+// Device address of g_error_sums_scratch on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address comes from
+// cudaGetSymbolAddress, once per device (the first call on a device may also
+// load this module onto it).
+static void* noalloc_scratch(int* status) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    *status = record_cuda_error(err);
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    *status = MXW_EUNSUPPORTED;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_error_sums_scratch);
+    if (err != cudaSuccess) {
+      *status = record_cuda_error(err);
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *status = MXW_OK;
+  return addr[dev];
+}
+
+}  // namespace mxw
+
+extern "C" int mxw_error_sums_noalloc(const void* original, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                      const void* reconstructed, int rdtype, int64_t rld, const uint8_t* packed,
+                                      const uint8_t* scales, const float* gamma, const float* hessian,
+                                      double* sums, void* stream) {
+  if (rows < 0 || cols <= 0) return MXW_EINVAL;
+  if (mxw_error_sums_workspace_size(rows, cols) > kNoAllocScratchBytes) return MXW_EUNSUPPORTED;
+  int status = MXW_OK;
+  void* scratch = noalloc_scratch(&status);
+  if (scratch == nullptr) return status;
+  // The ticket (first 16 bytes) must be zero when the kernel starts.  Each
+  // call leaves it zero, but clearing it on the caller's stream keeps every
+  // call independent of how an earlier one ended.  The partials need no
+  // clearing: every CTA overwrites its own before the fold reads them.
+  const cudaError_t err = cudaMemsetAsync(scratch, 0, 16, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return record_cuda_error(err);
+  return mxw_error_sums(original, dtype, rows, cols, ld, reconstructed, rdtype, rld, packed, scales, gamma, hessian,
+                        sums, scratch, kNoAllocScratchBytes, stream);
 }
