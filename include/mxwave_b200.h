@@ -141,6 +141,33 @@ MXW_API int mxw_error_sums_noalloc(const void* original, int dtype, int64_t rows
                                    void* stream);
 
 /*
+ * Routing-weighted squared activations per expert: for every route r (row
+ * route_rows[r] of x [rows, cols], row stride ld, squared router weight
+ * route_w2[r]) adds fl(fl(x^2) * w2) into squares[e][cols] of its expert e,
+ * and w2 into mass[e] (mass may be NULL).  Routes are grouped by expert:
+ * those of expert e are [offsets[e], offsets[e+1]) of the n_routes entries,
+ * in route order.  Sums are fp64 in route order, added once per expert and
+ * column (deterministic).  Rows outside x and offsets outside [0, n_routes]
+ * are ignored.
+ * Replaces the index_add_ accumulations of RoutedLayerMoments.update_inputs
+ * and update_down (mxwave/routed_calibration.py:104-141).
+ */
+MXW_API int mxw_accumulate_routed_squares(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                          const int64_t* route_rows, const float* route_w2, int64_t n_routes,
+                                          const int64_t* offsets, int64_t experts, float* squares, float* mass,
+                                          void* stream);
+
+/*
+ * Lossless repack of packed [rows, cols/2] MXFP4 codes and E8M0 scales
+ * [rows, cols/32] (compressed-tensors layout; packed 16-byte aligned) into
+ * ggml block_mxfp4 records: out[rows * cols/32 * 17] bytes, per block the
+ * scale byte then 16 bytes holding element j (low nibble) and j + 16 (high).
+ * Replaces repack_mxfp4_blocks (mxwave/gguf.py:134-150).
+ */
+MXW_API int mxw_repack_gguf_mxfp4(const uint8_t* packed, const uint8_t* scales, int64_t rows, int64_t cols,
+                                  uint8_t* out, void* stream);
+
+/*
  * Per-channel moments of activations x [tokens, cols] (row stride ld), added
  * into sum_abs[cols] (sum |x|) and sum_sq[cols] (sum x^2); either may be NULL.
  * Replaces the mean-abs / rms accumulation of ActivationCollector.update

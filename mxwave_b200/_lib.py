@@ -55,6 +55,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mxw_error_sums_workspace_size": (ctypes.c_size_t, [_i64, _i64]),
     "mxw_error_sums": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
                               ctypes.c_size_t, _vp]),
+    "mxw_accumulate_routed_squares": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _vp,
+                                             _vp]),
+    "mxw_repack_gguf_mxfp4": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "mxw_error_sums_noalloc": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _vp, _vp,
                                       _vp]),
 }

@@ -23,6 +23,10 @@ mxwave.calibration_stream.calibrate_decoder_sequentially
 mxwave.verify.sqnr / channel_weighted_sqnr / block_hessian_weighted_sqnr
   engine.py:447-458,565-585            mxwave_b200.verify (same names)
   expert_engine.py:620,776
+mxwave.routed_calibration.RoutedLayerMoments
+                                       mxwave_b200.routed_calibration.RoutedLayerMoments
+mxwave.gguf.repack_mxfp4_blocks        mxwave_b200.gguf.repack_mxfp4_blocks
+  gguf.py:349  kolibri_gguf.py:279
 =====================================  ============================================
 
 The engines keep their planning, durability, manifests and CLI; only the
@@ -52,7 +56,7 @@ class Installation:
 
 
 def _replacements() -> dict[str, dict[str, Any]]:
-    from . import calibration, calibration_stream, checkpoint, core, verify
+    from . import calibration, calibration_stream, checkpoint, core, gguf, routed_calibration, verify
 
     return {
         "mxwave.core": {
@@ -80,6 +84,10 @@ def _replacements() -> dict[str, dict[str, Any]]:
             "channel_weighted_sqnr": verify.channel_weighted_sqnr,
             "block_hessian_weighted_sqnr": verify.block_hessian_weighted_sqnr,
         },
+        "mxwave.routed_calibration": {"RoutedLayerMoments": routed_calibration.RoutedLayerMoments},
+        "mxwave.gguf": {"repack_mxfp4_blocks": gguf.repack_mxfp4_blocks},
+        "mxwave.kolibri_gguf": {"repack_mxfp4_blocks": gguf.repack_mxfp4_blocks},
+        "mxwave": {"repack_mxfp4_blocks": gguf.repack_mxfp4_blocks},
         "mxwave.checkpoint": {"iter_quantized_row_chunks": checkpoint.iter_quantized_row_chunks},
         "mxwave.shard": {"read_tensor_row_range": checkpoint.read_tensor_row_range},
         "mxwave.calibration": {

@@ -187,3 +187,37 @@ def sqnr_db(signal: float, noise: float) -> float:
     """10 log10(signal / noise) with both clamped below at fp32(1e-12), as verify.py does."""
     floor = float(np.float32(1e-12))
     return float(10.0 * np.log10(max(signal, floor) / max(noise, floor)))
+
+
+def routed_squares(inputs: np.ndarray, ids: np.ndarray, weights: np.ndarray, experts: int,
+                   token_major: bool) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """routed_calibration.py:104-141: per-expert sums of fl(fl(x^2) * fl(w^2)), float64.
+
+    token_major=False: route (t, k) reads row t (update_inputs); True: row r of
+    the flattened routes (update_down).  Returns (squares, mass, counts).
+    """
+    x = np.asarray(inputs, dtype=np.float32)
+    flat_ids = np.asarray(ids).reshape(-1).astype(np.int64)
+    w2 = np.square(np.asarray(weights, dtype=np.float32).reshape(-1))
+    top_k = np.asarray(ids).shape[1]
+    squares = np.zeros((experts, x.shape[1]))
+    mass = np.zeros(experts)
+    for r, e in enumerate(flat_ids):
+        row = x[r if token_major else r // top_k]
+        squares[e] += (np.square(row) * w2[r]).astype(np.float32)
+        mass[e] += w2[r]
+    return squares, mass, np.bincount(flat_ids, minlength=experts)
+
+
+def gguf_repack(packed: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """gguf.py:134-150: per block the scale byte, then code j | code j+16 << 4."""
+    p = np.asarray(packed, dtype=np.uint8)
+    rows, half = p.shape
+    blocks = half * 2 // 32
+    codes = np.empty((rows, half * 2), dtype=np.uint8)
+    codes[:, 0::2] = p & 0x0F
+    codes[:, 1::2] = p >> 4
+    codes = codes.reshape(rows, blocks, 32)
+    body = codes[:, :, :16] | (codes[:, :, 16:] << 4)
+    out = np.concatenate([np.asarray(scales, dtype=np.uint8).reshape(rows, blocks, 1), body], axis=-1)
+    return out.reshape(rows, blocks * 17)
