@@ -152,25 +152,41 @@ def run_ours(args) -> None:
     ev_q = []
 
     def step(record: bool) -> list:
+        cur = torch.cuda.current_stream(dev)  # the capture stream while a graph is recorded
         sum_sq.zero_()
         _lib.check(lib.mxw_accumulate_moments(x.data_ptr(), _lib.MXW_BF16, TOKENS, HIDDEN, HIDDEN, None,
-                                              sum_sq.data_ptr(), stream.cuda_stream), "moments")
+                                              sum_sq.data_ptr(), cur.cuda_stream), "moments")
         _lib.check(lib.mxw_finalize_moments(None, sum_sq.data_ptr(), HIDDEN, TOKENS, None, rms.data_ptr(),
-                                            stream.cuda_stream), "finalize")
+                                            cur.cuda_stream), "finalize")
         outs = []
         for w in ws:
             if record:
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
+                a.record(cur)
             outs.append(quantize_mxfp4(w, scale_percentile=PCT, gamma=rms, mse_clip_depth=DEPTH))
             if record:
-                b.record(stream)
+                b.record(cur)
                 ev_q.append((a, b))
         return outs
 
     for _ in range(args.warmup):
         step(False)
     torch.cuda.synchronize(dev)
+    # Per-launch duration of the quantize kernel (events around each launch).
+    for _ in range(max(3, args.steps // 2)):
+        step(True)
+    torch.cuda.synchronize(dev)
+    q_ms = sum(a.elapsed_time(b) for a, b in ev_q) / len(ev_q)
+    # The step as one CUDA graph: the same launches, without per-launch host
+    # overhead between them (the small moments/finalize kernels would
+    # otherwise wait on the Python side).
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(False)
+        graph.replay()
+        torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -179,7 +195,10 @@ def run_ours(args) -> None:
         time.sleep(0.3)
         start.record(stream)
         for _ in range(args.steps):
-            step(True)
+            if graph is not None:
+                graph.replay()
+            else:
+                step(False)
         stop.record(stream)
         torch.cuda.synchronize(dev)
     ms = start.elapsed_time(stop)
@@ -188,7 +207,7 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    q_ms = sum(a.elapsed_time(b) for a, b in ev_q) / len(ev_q)
+    del graph
 
     # ---- end to end through the public API, host pinned buffers.
     e2e = None if args.no_e2e else run_e2e(args, dev, world, rank)
@@ -222,7 +241,8 @@ def run_ours(args) -> None:
         "dtype": "f32 (bf16 in, u8 out)",
         "data": "synthetic (seeded on-device normal weights, heavy-channel activations)",
         "config": {"workload": WORKLOAD, "elements_per_step_per_gpu": elems, "l2": "inputs > L2 (356 MB weights)",
-                   "parallelism": f"tensor-sharded x{world}, no collective"},
+                   "parallelism": f"tensor-sharded x{world}, no collective",
+                   "launch": "one CUDA graph per step" if not args.no_graph else "eager launches"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
                      "traffic": args.traffic, "traffic_unit": "bytes per launch (ncu)",
@@ -465,6 +485,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-xtx", action="store_true", help="skip the X^T X calibration measurement")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--no-graph", action="store_true", help="launch the timed steps one kernel at a time")
     ap.add_argument("--traffic", type=float, default=QUANT_TRAFFIC_BYTES,
                     help="dram bytes per quantize launch from an ncu capture (recorded in the roofline)")
     args = ap.parse_args()
