@@ -251,7 +251,7 @@ def run_ours(args) -> None:
         "e2e": e2e,
         "cpu_baseline": cpu,
         "calibration_xtx": xtx,
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": 6 * args.steps,  # moments, finalize, 2 x (quantize + rare-block fixup)
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

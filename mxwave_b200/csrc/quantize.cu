@@ -60,6 +60,8 @@ enum QMode { kQAmax = 0, kQTop2 = 1, kQGeneral = 2 };
 
 struct QuantParams {
   int64_t rows, cols, nb, n_row_tiles, n_tiles;
+  const void* weight;  // the input again, for the rare blocks re-read from global memory
+  int64_t ld;
   const float* gamma;
   const float* hessian;
   uint8_t* packed;
@@ -243,9 +245,20 @@ __device__ __forceinline__ unsigned long long abs_dw2(unsigned long long nt, uns
 
 // Unweighted / gamma error of one candidate exponent e: mean over the block of
 // dW^2 (times gamma^2), core.py:224-234.
-template <bool GAMMA, bool UNFUSED>
+// gamma^2 pair j of the warp's block column from shared memory (every lane
+// reads the same address: a broadcast).  Volatile, so the loads stay inside
+// the candidate loop instead of being hoisted into 32 registers.
+__device__ __forceinline__ unsigned long long load_g2(const float* Gw, int j) {
+  unsigned long long v;
+  asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v) : "r"(smem_u32(Gw + 2 * j)));
+  return v;
+}
+
+// GS: gamma^2 pairs from shared memory (Gw) instead of registers (g2).
+template <bool GAMMA, bool UNFUSED, bool GS = false>
 __device__ __forceinline__ float candidate_error(const unsigned long long (&nt2)[16], int e,
-                                                 const unsigned long long (&g2)[16], unsigned long long NZ2) {
+                                                 const unsigned long long (&g2)[16], unsigned long long NZ2,
+                                                 const float* Gw = nullptr) {
   const float s = exp2i(e);
   const float ninv = -exp2i(-e);
   const unsigned long long S2 = pack2(s, s), NI2 = pack2(ninv, ninv);
@@ -258,7 +271,7 @@ __device__ __forceinline__ float candidate_error(const unsigned long long (&nt2)
       const unsigned long long d = abs_dw2<UNFUSED>(nt2[j], NI2, S2, NZ2);
       // fl(dW^2), then fl(fl(dW^2) * gamma^2): each product rounded before the add.
       unsigned long long sq = mul2_rounded(d, d, NZ2);
-      if constexpr (GAMMA) sq = mul2_rounded(sq, g2[j], NZ2);
+      if constexpr (GAMMA) sq = mul2_rounded(sq, GS ? load_g2(Gw, j) : g2[j], NZ2);
       p[lp] = (q == 0) ? sq : add2(p[lp], sq);
     }
   }
@@ -354,11 +367,21 @@ __device__ __forceinline__ int rtn_exponent(float block_max) {
 
 // Chooses the exponent and encodes one block into 16 packed bytes; returns the
 // E8M0 byte.  `Hs`: the block's Hessian (shared or global memory) or unused.
-template <int DT, int OBJ, int QM, bool HS_SHARED>
+// FAST (unweighted / gamma objectives of the TMA kernel): the candidate loop
+// carries only the fused error form.  A block with a candidate e >= 126,
+// where q * 2^e can overflow (largest magnitude near FLT_MAX), is left for
+// quantize_fixup_kernel: it gets the marker scale byte kRareBlock, which no
+// quantized block can have (scale bytes are 0..254).  Keeping the rare form
+// out of the hot loop saves registers and instructions there (5-7 % of
+// kernel time on B200).
+constexpr uint32_t kRareBlock = 255;
+
+template <int DT, int OBJ, int QM, bool HS_SHARED, bool GS = false, bool FAST = false>
 __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, const QuantParams& P,
                                                        const unsigned long long (&g2)[16], const float* Hs,
-                                                       uint4& packed) {
+                                                       uint4& packed, const float* Gw = nullptr) {
   int raw;
+  bool rare = false;  // FAST only: a candidate e >= 126 -> left for quantize_fixup_kernel
   if constexpr (OBJ == kObjRtn) {
     // core.py:240-243: the exponent is clamped to [-127, 127] before storage.
     raw = max(-127, min(127, rtn_exponent(B.amax)));
@@ -398,6 +421,11 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
     // no-clipping exponent unless it repeats one of them.
     const int n_seq = hi_e - lo_e + 1;
     const bool safe_new = safe_e < lo_e || safe_e > hi_e;
+    if constexpr (FAST) {
+      // No early exit (it would split the hot path): the block runs on with
+      // the fused form and only its scale byte becomes the marker.
+      rare = (safe_new ? max(hi_e, safe_e) : hi_e) >= 126;
+    }
     for (int k = 0; k < n_seq + (safe_new ? 1 : 0); ++k) {
       const int e = k < n_seq ? lo_e + k : safe_e;
       // q * 2^e can overflow only for e >= 126: that rare case takes the
@@ -407,8 +435,12 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
         err = e < 126 ? candidate_error_hessian<DT, HS_SHARED, false>(B, e, Hs, NZ2)
                       : candidate_error_hessian<DT, HS_SHARED, true>(B, e, Hs, NZ2);
       } else {
-        err = e < 126 ? candidate_error<OBJ == kObjGamma, false>(B.nt2, e, g2, NZ2)
-                      : candidate_error<OBJ == kObjGamma, true>(B.nt2, e, g2, NZ2);
+        if constexpr (FAST) {
+          err = candidate_error<OBJ == kObjGamma, false, GS>(B.nt2, e, g2, NZ2, Gw);
+        } else {
+          err = e < 126 ? candidate_error<OBJ == kObjGamma, false, GS>(B.nt2, e, g2, NZ2, Gw)
+                        : candidate_error<OBJ == kObjGamma, true, GS>(B.nt2, e, g2, NZ2, Gw);
+        }
       }
       if (err < best) raw = e;
       best = (isnan(err) || isnan(best)) ? __int_as_float(0x7fffffff) : fminf(best, err);
@@ -430,21 +462,18 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
   packed.z = __byte_perm(__byte_perm(bytes[8], bytes[9], 0x0040), __byte_perm(bytes[10], bytes[11], 0x0040), 0x5410);
   packed.w =
       __byte_perm(__byte_perm(bytes[12], bytes[13], 0x0040), __byte_perm(bytes[14], bytes[15], 0x0040), 0x5410);
-  return static_cast<uint32_t>(raw + 127);
+  return rare ? kRareBlock : static_cast<uint32_t>(raw + 127);
 }
 
 // Per-warp block-column state: gamma^2 pairs in registers, Hessian in smem.
 template <int OBJ>
-__device__ __forceinline__ void load_column_state(const QuantParams& P, int64_t b, int lane, float* Hw,
-                                                  unsigned long long (&g2)[16]) {
+__device__ __forceinline__ void load_column_state(const QuantParams& P, int64_t b, int lane, float* Hw, float* Gw) {
   if constexpr (OBJ == kObjGamma) {
-    const float4* gp = reinterpret_cast<const float4*>(P.gamma + b * kBlock);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 g = __ldg(gp + j);
-      g2[2 * j] = pack2(__fmul_rn(g.x, g.x), __fmul_rn(g.y, g.y));
-      g2[2 * j + 1] = pack2(__fmul_rn(g.z, g.z), __fmul_rn(g.w, g.w));
-    }
+    // gamma^2 of the warp's 32 columns, one per lane, in shared memory.
+    __syncwarp();
+    const float g = __ldg(P.gamma + b * kBlock + lane);
+    Gw[lane] = __fmul_rn(g, g);
+    __syncwarp();
   }
   if constexpr (OBJ == kObjHess) {
     __syncwarp();
@@ -468,8 +497,9 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   uint8_t* out_stage = smem + kStages * kStageBytes;               // [ring][32 rows][128 B], 128B-swizzled
   uint8_t* scale_stage = out_stage + kOutBuffers * kOutTileBytes;  // [ring][32 rows][8 B]
   float* Hs = reinterpret_cast<float*>(scale_stage + kOutBuffers * kScaleTileBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(Hs) +
-                                               (OBJ == kObjHess ? kTileBlocks * 1024 * 4 : 0));
+  float* Gs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(Hs) + (OBJ == kObjHess ? kTileBlocks * 1024 * 4 : 0));
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(Gs) + (OBJ == kObjGamma ? kTileBlocks * kBlock * 4 : 0));
   uint64_t* empty = full + kStages;
   uint64_t* out_full = empty + kStages;
   uint64_t* out_empty = out_full + kOutBuffers;
@@ -566,8 +596,9 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   }
 
   // ---------------- consumer warps: warp w owns block column strip*8 + w.
-  unsigned long long g2[16];
+  unsigned long long g2[16];  // unused here: gamma^2 lives in shared memory (Gw)
   float* Hw = Hs + warp * 1024;
+  float* Gw = Gs + warp * kBlock;
   int64_t cur_strip = -1;
   bool valid_col = false;
   int64_t b = 0;
@@ -579,7 +610,7 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       cur_strip = strip;
       b = strip * kTileBlocks + warp;
       valid_col = b < P.nb;
-      if (valid_col) load_column_state<OBJ>(P, b, lane, Hw, g2);
+      if (valid_col) load_column_state<OBJ>(P, b, lane, Hw, Gw);
     }
     const int s = static_cast<int>(it % kStages);
     // Warp-uniform verdict: a lane that timed out takes the whole warp out.
@@ -599,7 +630,7 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       if (lane == 0) mbar_arrive(&empty[s]);
       if (rt * kTileRows + lane < P.rows) {
         any_nonfinite |= B.nonfinite;
-        sc = quantize_one_block<DT, OBJ, QM, true>(B, P, g2, Hw, pk);
+        sc = quantize_one_block<DT, OBJ, QM, true, true, OBJ != kObjHess>(B, P, g2, Hw, pk, Gw);
       }
     } else {
       __syncwarp();
@@ -619,6 +650,87 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
     if (lane == 0) mbar_arrive(&out_full[buf]);
   }
   if (P.flags && __any_sync(0xffffffffu, any_nonfinite) && lane == 0) atomicOr(P.flags, MXW_FLAG_NONFINITE);
+}
+
+// ------------------------------------------------------ rare-block fixup
+
+// One block read from global memory as fp32 (exact for every input type) and
+// quantized with both error forms available (see quantize_one_block).
+template <int DT, int OBJ, int QM>
+__device__ __forceinline__ uint32_t quantize_block_slow(const QuantParams& P, int64_t row, int64_t blk, uint4* packed) {
+  BlockData<MXW_F32> B;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int64_t i = row * P.ld + blk * kBlock + 2 * j;
+    float x0, x1;
+    if constexpr (DT == MXW_BF16) {
+      const uint16_t* p = static_cast<const uint16_t*>(P.weight) + i;
+      x0 = bits_f32(static_cast<uint32_t>(p[0]) << 16);
+      x1 = bits_f32(static_cast<uint32_t>(p[1]) << 16);
+    } else if constexpr (DT == MXW_F16) {
+      const __half* p = static_cast<const __half*>(P.weight) + i;
+      x0 = __half2float(p[0]);
+      x1 = __half2float(p[1]);
+    } else {
+      const float* p = static_cast<const float*>(P.weight) + i;
+      x0 = p[0];
+      x1 = p[1];
+    }
+    B.t2[j] = pack2(x0, x1);
+  }
+  finish_stats_f32<MXW_F32, QM>(B, B.t2);
+  unsigned long long g2[16];
+  if constexpr (OBJ == kObjGamma) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float ga = P.gamma[blk * kBlock + 2 * j], gb = P.gamma[blk * kBlock + 2 * j + 1];
+      g2[j] = pack2(__fmul_rn(ga, ga), __fmul_rn(gb, gb));
+    }
+  }
+  uint4 pk;
+  const uint32_t sc = quantize_one_block<MXW_F32, OBJ, QM, false>(B, P, g2, nullptr, pk);
+  *packed = pk;
+  return sc;
+}
+
+// Runs after quantize_tma_kernel (unweighted / gamma objectives, same stream):
+// finds the blocks it marked kRareBlock and quantizes them in full.  Each
+// thread checks kFixupPer consecutive scale bytes with independent loads (one
+// pass over 1 byte per 32 weights); marked blocks are rare.
+constexpr int kFixupPer = 16;
+
+template <int DT, int OBJ, int QM>
+__global__ void __launch_bounds__(256) quantize_fixup_kernel(const QuantParams P) {
+  const int64_t total = P.rows * P.nb;
+  const int64_t first = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * kFixupPer;
+  if (first >= total) return;
+  uint32_t marked = 0;
+  if (first + kFixupPer <= total && reinterpret_cast<uintptr_t>(P.scales + first) % 16 == 0) {
+    const uint4 v = *reinterpret_cast<const uint4*>(P.scales + first);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t m = __vcmpeq4(w[q], 0xffffffffu);  // 0xff per marked byte
+      if (m) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if ((m >> (8 * k)) & 1u) marked |= 1u << (4 * q + k);
+      }
+    }
+  } else {
+    for (int k = 0; k < kFixupPer; ++k)
+      if (first + k < total && P.scales[first + k] == kRareBlock) marked |= 1u << k;
+  }
+  while (marked) {
+    const int k = __ffs(marked) - 1;
+    marked &= marked - 1;
+    const int64_t idx = first + k;
+    const int64_t r = idx / P.nb, b = idx % P.nb;
+    uint4 pk;
+    const uint32_t sc = quantize_block_slow<DT, OBJ, QM>(P, r, b, &pk);
+    *reinterpret_cast<uint4*>(P.packed + r * (P.cols / 2) + b * 16) = pk;
+    P.scales[idx] = static_cast<uint8_t>(sc);
+  }
 }
 
 // -------------------------------------------------- generic (unaligned) path
@@ -694,7 +806,8 @@ static LaunchInfo& launch_info(const void* kern, int dev) {
 template <int DT, int OBJ, int QM>
 static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStream_t stream) {
   const size_t smem = 1024 + kStages * Elem<DT>::kStageBytes + kOutBuffers * (kOutTileBytes + kScaleTileBytes) +
-                      (OBJ == kObjHess ? kTileBlocks * 4096 : 0) + (2 * kStages + 2 * kOutBuffers) * sizeof(uint64_t);
+                      (OBJ == kObjHess ? kTileBlocks * 4096 : 0) + (OBJ == kObjGamma ? kTileBlocks * kBlock * 4 : 0) +
+                      (2 * kStages + 2 * kOutBuffers) * sizeof(uint64_t);
   CUtensorMap map;
   const CUtensorMapDataType dt = DT == MXW_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : DT == MXW_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -724,7 +837,16 @@ static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStre
   P.n_tiles = ((P.nb + kTileBlocks - 1) / kTileBlocks) * P.n_row_tiles;
   const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(P.n_tiles, static_cast<int64_t>(num_sms()) * li.per_sm));
   kern<<<static_cast<unsigned>(ctas), kQuantThreads, smem, stream>>>(map, out_map, P);
-  return check_launch();
+  const int rc = check_launch();
+  if constexpr (OBJ == kObjNone || OBJ == kObjGamma) {
+    if (rc != MXW_OK) return rc;
+    const int64_t threads = (P.rows * P.nb + kFixupPer - 1) / kFixupPer;
+    const int64_t blocks = (threads + 255) / 256;
+    if (blocks > 0x7fffffff) return MXW_EUNSUPPORTED;
+    quantize_fixup_kernel<DT, OBJ, QM><<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, stream>>>(P);
+    return check_launch();
+  }
+  return rc;
 }
 
 template <int DT, int OBJ, int QM>
@@ -788,6 +910,8 @@ extern "C" int mxw_quantize_mxfp4(const void* weight, int dtype, int64_t rows, i
   QuantParams P{};
   P.rows = rows;
   P.cols = cols;
+  P.weight = weight;
+  P.ld = ld;
   P.nb = cols / kBlock;
   P.n_row_tiles = (rows + kTileRows - 1) / kTileRows;
   P.gamma = gamma;

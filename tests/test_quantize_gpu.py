@@ -279,3 +279,29 @@ def test_block_hessian_reference_sha(cuda_device) -> None:
     p, s = quantize_mxfp4(_to_device(w4, cuda_device), hessian=h4, mse_clip_depth=1)
     assert _sha(p) == c["packed_sha256"]
     assert _sha(s) == c["scales_sha256"]
+
+
+@pytest.mark.parametrize("objective", ["none", "gamma"])
+@pytest.mark.parametrize("depth", [1, 4])
+def test_near_flt_max_blocks_in_a_large_tensor(objective, depth, cuda_device) -> None:
+    """Blocks whose candidates reach e >= 126 (magnitudes near FLT_MAX) are
+    finished by the rare-block pass; the rest of the tensor takes the fast
+    path.  Bytes must match the oracle everywhere."""
+    rows, cols = 96, 2048
+    w = syn.det_dense_weight(rows, cols, 77 + depth, outlier_fraction=0.01)
+    f = syn.bf16_bits_to_f32(w).copy()
+    rng = np.random.default_rng(5)
+    for r, b in zip(rng.integers(0, rows, 40), rng.integers(0, cols // 32, 40)):
+        mag = rng.uniform(0.3e38, 1.6e38)  # block maxima from ~1e38 up to the bf16 limit
+        f[r, 32 * b: 32 * b + 32] = np.clip(rng.standard_normal(32) * mag, -3.3e38, 3.3e38).astype(np.float32)
+    bits = syn.f32_to_bf16_bits(f)
+    kw: dict = {"mse_clip_depth": depth}
+    okw: dict = {"mse_clip_depth": depth}
+    if objective == "gamma":
+        g = syn.det_channel_scales(cols, 9).astype(np.float32)
+        kw["gamma"], okw["gamma"] = torch.from_numpy(g).to(cuda_device), g
+    p, s = _gpu(_to_device(bits, cuda_device), cuda_device, **kw)
+    po, so = oracle.quantize_mxfp4(bits, **okw)
+    block_max = np.abs(syn.bf16_bits_to_f32(bits)).reshape(rows, cols // 32, 32).max(axis=-1)
+    assert (block_max > 6.0 * 2.0 ** 125).any(), "the case must contain blocks with e >= 126 candidates"
+    assert_same_bytes(bits, p, s, po, so)
