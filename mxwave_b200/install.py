@@ -27,6 +27,9 @@ mxwave.routed_calibration.RoutedLayerMoments
                                        mxwave_b200.routed_calibration.RoutedLayerMoments
 mxwave.gguf.repack_mxfp4_blocks        mxwave_b200.gguf.repack_mxfp4_blocks
   gguf.py:349  kolibri_gguf.py:279
+mxwave.calibration.save_calibration_data / open_calibration_data
+  calibration_cli.py:474  engine.py:500
+                                       mxwave_b200.calibration_artifact (device hand-off)
 =====================================  ============================================
 
 The engines keep their planning, durability, manifests and CLI; only the
@@ -56,7 +59,7 @@ class Installation:
 
 
 def _replacements() -> dict[str, dict[str, Any]]:
-    from . import calibration, calibration_stream, checkpoint, core, gguf, routed_calibration, verify
+    from . import calibration, calibration_artifact, calibration_stream, checkpoint, core, gguf, routed_calibration, verify
 
     return {
         "mxwave.core": {
@@ -72,6 +75,7 @@ def _replacements() -> dict[str, dict[str, Any]]:
             "sqnr": verify.sqnr,
             "channel_weighted_sqnr": verify.channel_weighted_sqnr,
             "block_hessian_weighted_sqnr": verify.block_hessian_weighted_sqnr,
+            "open_calibration_data": calibration_artifact.open_calibration_data,
         },
         "mxwave.expert_engine": {
             "quantize_mxfp4": core.quantize_mxfp4,
@@ -93,6 +97,8 @@ def _replacements() -> dict[str, dict[str, Any]]:
         "mxwave.calibration": {
             "ActivationCollector": calibration.ActivationCollector,
             "attach_activation_hooks": calibration.attach_activation_hooks,
+            "save_calibration_data": calibration_artifact.save_calibration_data,
+            "open_calibration_data": calibration_artifact.open_calibration_data,
         },
         "mxwave.calibration_stream": {
             "ActivationCollector": calibration.ActivationCollector,
@@ -101,6 +107,7 @@ def _replacements() -> dict[str, dict[str, Any]]:
         },
         "mxwave.calibration_cli": {
             "calibrate_decoder_sequentially": calibration_stream.calibrate_decoder_sequentially,
+            "save_calibration_data": calibration_artifact.save_calibration_data,
         },
     }
 
@@ -120,6 +127,10 @@ def install() -> Installation:
             modules[module_name] = importlib.import_module(module_name)
         except ImportError:
             continue
+    if "mxwave.calibration" in modules:
+        from . import calibration_artifact
+
+        calibration_artifact._capture_originals()  # it calls the reference's own writer/reader
     for module_name, names in _replacements().items():
         module = modules.get(module_name)
         if module is None:
