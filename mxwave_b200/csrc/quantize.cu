@@ -694,42 +694,53 @@ __device__ __forceinline__ uint32_t quantize_block_slow(const QuantParams& P, in
 }
 
 // Runs after quantize_tma_kernel (unweighted / gamma objectives, same stream):
-// finds the blocks it marked kRareBlock and quantizes them in full.  Each
-// thread checks kFixupPer consecutive scale bytes with independent loads (one
-// pass over 1 byte per 32 weights); marked blocks are rare.
-constexpr int kFixupPer = 16;
+// finds the blocks it marked kRareBlock and quantizes them in full.  One wave
+// of threads reads the scale bytes once (1 byte per 32 weights) in 16-byte
+// chunks, four independent loads in flight per thread; marked blocks are rare.
+constexpr int kFixupChunk = 16;
+
+template <int DT, int OBJ, int QM>
+__device__ __forceinline__ void fixup_block(const QuantParams& P, int64_t idx) {
+  const int64_t r = idx / P.nb, b = idx % P.nb;
+  uint4 pk;
+  const uint32_t sc = quantize_block_slow<DT, OBJ, QM>(P, r, b, &pk);
+  *reinterpret_cast<uint4*>(P.packed + r * (P.cols / 2) + b * 16) = pk;
+  P.scales[idx] = static_cast<uint8_t>(sc);
+}
 
 template <int DT, int OBJ, int QM>
 __global__ void __launch_bounds__(256) quantize_fixup_kernel(const QuantParams P) {
   const int64_t total = P.rows * P.nb;
-  const int64_t first = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) * kFixupPer;
-  if (first >= total) return;
-  uint32_t marked = 0;
-  if (first + kFixupPer <= total && reinterpret_cast<uintptr_t>(P.scales + first) % 16 == 0) {
-    const uint4 v = *reinterpret_cast<const uint4*>(P.scales + first);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (reinterpret_cast<uintptr_t>(P.scales) % 16 == 0) {
+    const int64_t chunks = total / kFixupChunk;
+    for (int64_t c0 = tid; c0 < chunks; c0 += 4 * stride) {
+      uint4 v[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t m = __vcmpeq4(w[q], 0xffffffffu);  // 0xff per marked byte
-      if (m) {
+      for (int u = 0; u < 4; ++u) {
+        const int64_t c = c0 + u * stride;
+        v[u] = c < chunks ? *reinterpret_cast<const uint4*>(P.scales + c * kFixupChunk) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if ((m >> (8 * k)) & 1u) marked |= 1u << (4 * q + k);
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t m = __vcmpeq4(w[q], 0xffffffffu);  // 0xff per marked byte
+          if (m) {
+            for (int k = 0; k < 4; ++k)
+              if ((m >> (8 * k)) & 1u) fixup_block<DT, OBJ, QM>(P, (c0 + u * stride) * kFixupChunk + 4 * q + k);
+          }
+        }
       }
     }
+    // The tail beyond the last whole chunk.
+    for (int64_t i = chunks * kFixupChunk + tid; i < total; i += stride)
+      if (P.scales[i] == kRareBlock) fixup_block<DT, OBJ, QM>(P, i);
   } else {
-    for (int k = 0; k < kFixupPer; ++k)
-      if (first + k < total && P.scales[first + k] == kRareBlock) marked |= 1u << k;
-  }
-  while (marked) {
-    const int k = __ffs(marked) - 1;
-    marked &= marked - 1;
-    const int64_t idx = first + k;
-    const int64_t r = idx / P.nb, b = idx % P.nb;
-    uint4 pk;
-    const uint32_t sc = quantize_block_slow<DT, OBJ, QM>(P, r, b, &pk);
-    *reinterpret_cast<uint4*>(P.packed + r * (P.cols / 2) + b * 16) = pk;
-    P.scales[idx] = static_cast<uint8_t>(sc);
+    for (int64_t i = tid; i < total; i += stride)
+      if (P.scales[i] == kRareBlock) fixup_block<DT, OBJ, QM>(P, i);
   }
 }
 
@@ -840,9 +851,8 @@ static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStre
   const int rc = check_launch();
   if constexpr (OBJ == kObjNone || OBJ == kObjGamma) {
     if (rc != MXW_OK) return rc;
-    const int64_t threads = (P.rows * P.nb + kFixupPer - 1) / kFixupPer;
-    const int64_t blocks = (threads + 255) / 256;
-    if (blocks > 0x7fffffff) return MXW_EUNSUPPORTED;
+    const int64_t chunks = (P.rows * P.nb + kFixupChunk - 1) / kFixupChunk;
+    const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()) * 2);
     quantize_fixup_kernel<DT, OBJ, QM><<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, stream>>>(P);
     return check_launch();
   }
