@@ -173,21 +173,38 @@ __device__ __forceinline__ void finish_stats_f32(BlockData<DT>& B, const unsigne
   B.second = bits_f32(m2);
 }
 
+// The 16 words (32 two-byte elements) of the block in tile row `lane`, block
+// column `w`, from a 128B-swizzled stage.
+__device__ __forceinline__ void stage_words(const uint8_t* stage, int w, int lane, uint32_t (&words)[16]) {
+  const uint8_t* box = stage + (w >> 1) * kBoxBytes + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = (4 * (w & 1) + j) ^ (lane & 7);
+    const uint4 v = *reinterpret_cast<const uint4*>(box + (c << 4));
+    words[4 * j + 0] = v.x;
+    words[4 * j + 1] = v.y;
+    words[4 * j + 2] = v.z;
+    words[4 * j + 3] = v.w;
+  }
+}
+
+// Signed element pair of a word of two 2-byte elements, as fp32.
+template <int DT>
+__device__ __forceinline__ unsigned long long word_pair(uint32_t w) {
+  if constexpr (DT == MXW_BF16) {
+    return pack2(bits_f32(w << 16), bits_f32(w & 0xffff0000u));
+  } else {
+    const __half2 h = *reinterpret_cast<const __half2*>(&w);
+    return pack2(__low2float(h), __high2float(h));
+  }
+}
+
 // Read this thread's block (row `lane` of the tile, block column `w`) from a
 // swizzled stage.
 template <int DT, int QM>
 __device__ __forceinline__ void read_block_smem(const uint8_t* stage, int w, int lane, BlockData<DT>& B) {
   if constexpr (Elem<DT>::kBytes == 2) {
-    const uint8_t* box = stage + (w >> 1) * kBoxBytes + lane * 128;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = (4 * (w & 1) + j) ^ (lane & 7);
-      const uint4 v = *reinterpret_cast<const uint4*>(box + (c << 4));
-      B.words[4 * j + 0] = v.x;
-      B.words[4 * j + 1] = v.y;
-      B.words[4 * j + 2] = v.z;
-      B.words[4 * j + 3] = v.w;
-    }
+    stage_words(stage, w, lane, B.words);
     finish_stats_16bit<DT, QM>(B);
   } else {
     const uint8_t* box = stage + w * kBoxBytes + lane * 128;
@@ -376,6 +393,76 @@ __device__ __forceinline__ int rtn_exponent(float block_max) {
 // kernel time on B200).
 constexpr uint32_t kRareBlock = 255;
 
+// Final encode (core.py:242-249): x = clamp(t / 2^raw) -> nibble, -0 -> code 0.
+// `pair(j)` yields the signed element pair j as fp32.
+template <typename PairFn>
+__device__ __forceinline__ void encode_pairs(PairFn pair, const QuantParams& P, int raw, uint4& packed) {
+  const float inv = exp2i(-raw);
+  const unsigned long long I2 = pack2(inv, inv);
+  const unsigned long long Z2 = pack2(P.zero, P.zero);
+  const unsigned long long NZ2e = pack2(P.negzero, P.negzero);
+  uint32_t bytes[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const f2 x = unpack2(add2(mul2_rounded(pair(j), I2, NZ2e), Z2));
+    bytes[j] = e2m1x2(x.x, x.y);
+  }
+  packed.x = __byte_perm(__byte_perm(bytes[0], bytes[1], 0x0040), __byte_perm(bytes[2], bytes[3], 0x0040), 0x5410);
+  packed.y = __byte_perm(__byte_perm(bytes[4], bytes[5], 0x0040), __byte_perm(bytes[6], bytes[7], 0x0040), 0x5410);
+  packed.z = __byte_perm(__byte_perm(bytes[8], bytes[9], 0x0040), __byte_perm(bytes[10], bytes[11], 0x0040), 0x5410);
+  packed.w =
+      __byte_perm(__byte_perm(bytes[12], bytes[13], 0x0040), __byte_perm(bytes[14], bytes[15], 0x0040), 0x5410);
+}
+
+template <int DT>
+__device__ __forceinline__ void encode_block(const BlockData<DT>& B, const QuantParams& P, int raw, uint4& packed) {
+  encode_pairs([&](int j) { return B.signed_pair(j); }, P, raw, packed);
+}
+
+// The percentile anchor of a block (core.py:183-189): amax, or torch.quantile
+// by linear interpolation between two order statistics.
+template <int QM>
+__device__ __forceinline__ float block_anchor(float amax, float second, const unsigned long long (&nt2)[16],
+                                              const QuantParams& P) {
+  if constexpr (QM == kQAmax) {
+    return amax;
+  } else {
+    float lo, hi;
+    if constexpr (QM == kQTop2) {
+      lo = P.q_below == 31 ? amax : second;
+      hi = P.q_above == 31 ? amax : second;
+    } else {
+      lo = kth_magnitude(nt2, P.q_below);
+      hi = (P.q_above == P.q_below) ? lo : kth_magnitude(nt2, P.q_above);
+    }
+    const float d = __fsub_rn(hi, lo);
+    return P.q_small ? __fmaf_rn(P.q_w, d, lo) : __fmaf_rn(__fsub_rn(P.q_w, 1.0f), d, hi);
+  }
+}
+
+// floor(torch.log2(x / 6)) and ceil(torch.log2(y / 6)) in fp32 for finite
+// x >= 1e-6 and y >= 1e-12, without the division.  With x = m * 2^E, fl(x/6)
+// lies in [2^(E-2), 2^(E-1)) for m >= 1.5 and in (2^(E-3), 2^(E-2)) below
+// (the rounded quotient never reaches the power of two).  torch's fp32 log2
+// can round to an integer only when the quotient is within 256 ulps of a
+// power of two: for floor that is m within 256 ulps under 1.5, for ceil m
+// within 512 ulps over 1.5; those take the division and the exact test.
+// Agreement with the division-based definition outside the bands was checked
+// on the CPU for every fp32 value in range (oracle/check_exponents.c).
+__device__ __forceinline__ int floor_log2_div6(float x) {
+  const uint32_t b = f32_bits(x);
+  const uint32_t man = b & 0x7fffffu;
+  if (man - (0x400000u - 256u) < 256u || b >= 0x7f800000u) return floor_log2_f32(__fdiv_rn(x, 6.0f));
+  return static_cast<int>(b >> 23) - 127 - (man >= 0x400000u ? 2 : 3);
+}
+
+__device__ __forceinline__ int ceil_log2_div6(float y) {
+  const uint32_t b = f32_bits(y);
+  const uint32_t man = b & 0x7fffffu;
+  if (man - 0x400001u < 512u || b >= 0x7f800000u) return ceil_log2_f32(__fdiv_rn(y, 6.0f));
+  return static_cast<int>(b >> 23) - 127 - (man > 0x400000u ? 1 : 2);
+}
+
 template <int DT, int OBJ, int QM, bool HS_SHARED, bool GS = false, bool FAST = false>
 __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, const QuantParams& P,
                                                        const unsigned long long (&g2)[16], const float* Hs,
@@ -386,24 +473,10 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
     // core.py:240-243: the exponent is clamped to [-127, 127] before storage.
     raw = max(-127, min(127, rtn_exponent(B.amax)));
   } else {
-    float anchor;
-    if constexpr (QM == kQAmax) {
-      anchor = B.amax;
-    } else {
-      float lo, hi;
-      if constexpr (QM == kQTop2) {
-        lo = P.q_below == 31 ? B.amax : B.second;
-        hi = P.q_above == 31 ? B.amax : B.second;
-      } else {
-        lo = kth_magnitude(B.nt2, P.q_below);
-        hi = (P.q_above == P.q_below) ? lo : kth_magnitude(B.nt2, P.q_above);
-      }
-      const float d = __fsub_rn(hi, lo);
-      anchor = P.q_small ? __fmaf_rn(P.q_w, d, lo) : __fmaf_rn(__fsub_rn(P.q_w, 1.0f), d, hi);
-    }
+    float anchor = block_anchor<QM>(B.amax, B.second, B.nt2, P);
     const bool near_zero = B.amax < 1e-6f;
     anchor = fmaxf(anchor, 1e-6f);
-    const int floor_e = floor_log2_f32(__fdiv_rn(anchor, 6.0f));
+    const int floor_e = floor_log2_div6(anchor);
     const int lo_e = max(-127, min(127, floor_e - P.depth));
     if (near_zero) {
       // t is replaced by zeros (core.py:194-195): every candidate has error 0,
@@ -412,7 +485,7 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
       return static_cast<uint32_t>(lo_e + 127);
     }
     const int hi_e = max(-127, min(127, floor_e + 1));
-    const int safe_e = max(-127, min(127, ceil_log2_f32(__fdiv_rn(fmaxf(B.amax, 1e-12f), 6.0f))));
+    const int safe_e = max(-127, min(127, ceil_log2_div6(fmaxf(B.amax, 1e-12f))));
     const unsigned long long NZ2 = pack2(P.negzero, P.negzero);
     float best = __int_as_float(0x7f800000);
     raw = lo_e;
@@ -446,33 +519,27 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
       best = (isnan(err) || isnan(best)) ? __int_as_float(0x7fffffff) : fminf(best, err);
     }
   }
-  // Final encode (core.py:242-249): x = clamp(t / 2^raw) -> nibble, -0 -> code 0.
-  const float inv = exp2i(-raw);
-  const unsigned long long I2 = pack2(inv, inv);
-  const unsigned long long Z2 = pack2(P.zero, P.zero);
-  const unsigned long long NZ2e = pack2(P.negzero, P.negzero);
-  uint32_t bytes[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const f2 x = unpack2(add2(mul2_rounded(B.signed_pair(j), I2, NZ2e), Z2));
-    bytes[j] = e2m1x2(x.x, x.y);
-  }
-  packed.x = __byte_perm(__byte_perm(bytes[0], bytes[1], 0x0040), __byte_perm(bytes[2], bytes[3], 0x0040), 0x5410);
-  packed.y = __byte_perm(__byte_perm(bytes[4], bytes[5], 0x0040), __byte_perm(bytes[6], bytes[7], 0x0040), 0x5410);
-  packed.z = __byte_perm(__byte_perm(bytes[8], bytes[9], 0x0040), __byte_perm(bytes[10], bytes[11], 0x0040), 0x5410);
-  packed.w =
-      __byte_perm(__byte_perm(bytes[12], bytes[13], 0x0040), __byte_perm(bytes[14], bytes[15], 0x0040), 0x5410);
+  encode_block(B, P, raw, packed);
   return rare ? kRareBlock : static_cast<uint32_t>(raw + 127);
 }
 
-// Per-warp block-column state: gamma^2 pairs in registers, Hessian in smem.
+// Per-warp block-column state in shared memory: gamma^2 (fp32, then the same
+// values as bf16x2 pairs for the clipping bound) or the block Hessian.
+constexpr int kGammaWords = kBlock + kBlock / 2;
+
 template <int OBJ>
 __device__ __forceinline__ void load_column_state(const QuantParams& P, int64_t b, int lane, float* Hw, float* Gw) {
   if constexpr (OBJ == kObjGamma) {
-    // gamma^2 of the warp's 32 columns, one per lane, in shared memory.
     __syncwarp();
     const float g = __ldg(P.gamma + b * kBlock + lane);
-    Gw[lane] = __fmul_rn(g, g);
+    const float g2 = __fmul_rn(g, g);
+    Gw[lane] = g2;
+    const float g2n = __shfl_down_sync(0xffffffffu, g2, 1);
+    if ((lane & 1) == 0) {
+      uint32_t pr;
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pr) : "f"(g2n), "f"(g2));
+      reinterpret_cast<uint32_t*>(Gw + kBlock)[lane >> 1] = pr;
+    }
     __syncwarp();
   }
   if constexpr (OBJ == kObjHess) {
@@ -484,7 +551,351 @@ __device__ __forceinline__ void load_column_state(const QuantParams& P, int64_t 
   }
 }
 
+// ------------------------------------------------ two-candidate fast path
+//
+// 2-byte inputs, top-2 or amax anchor.  The reference's candidate order is
+// f-depth, ..., f-1, f, f+1 and then the no-clipping exponent `safe` when it
+// is new (core.py:201-209).  With an anchor at or below the block maximum,
+// safe >= f, so it is new only as f+2 or higher.  Each thread evaluates its
+// own block's f and f+1 errors exactly, in one pass that also yields each
+// candidate's codes.  The clipping candidates below f are dropped when a lower
+// bound on the error of f-1 certifiably exceeds min(E_f, E_f+1): the bound
+// grows as the clip threshold falls, so it covers every deeper candidate too,
+// and a strictly larger error never wins the strict-< argmin.  The blocks the
+// bound does not decide, and the blocks whose safe exponent is f+2, get those
+// candidates evaluated exactly by the whole warp together: lane = element,
+// read from the tile still held in shared memory, with the reference's
+// summation order kept through shuffles.  Blocks outside the path's
+// preconditions (non-finite values, block scales of 2^15 and above,
+// safe >= f+3, NaN errors) take the rare marker and are finished by
+// quantize_fixup_kernel.
+
+template <int DT, int OBJ, int QM>
+struct FastPath {
+  static constexpr bool value = Elem<DT>::kBytes == 2 && OBJ == kObjNone && (QM == kQTop2 || QM == kQAmax);
+};
+
+__device__ __forceinline__ float nan_min(float best, float err) {
+  return (isnan(err) || isnan(best)) ? __int_as_float(0x7fffffff) : fminf(best, err);
+}
+
+// Certified "E_{f-1} > E_hi" from a computed lower bound `lb` of E_{f-1}.
+// lb is at most 1.09x the exact sum it bounds (at most 21 roundings of 2^-8
+// each in bf16 arithmetic; fp32 is tighter) and the reference's fp32 error is
+// at least (1 - 2^-20)x the exact sum once it is far above the subnormal
+// range, so 7/8 of lb is a strict lower bound there.
+__device__ __forceinline__ bool lb_prunes(float lb, float e_hi) {
+  const float l = __fmul_rn(lb, 0.875f);
+  return l > e_hi && l >= 0x1p-100f && lb < __int_as_float(0x7f800000);
+}
+
+// sum over the block of g2_i * max(|t_i| - c, 0)^2, in bf16x2 arithmetic
+// (bf16 inputs).  c = 3 * 2^f has two significant bits, so -c is exact in bf16.
+template <bool GAMMA>
+__device__ __forceinline__ float clip_excess_bf16(const uint32_t (&words)[16], float c, const uint32_t* G2b) {
+  const uint32_t nc = (f32_bits(-c) >> 16) * 0x00010001u;
+  const uint32_t one = 0x3f803f80u;
+  uint32_t acc = 0u;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t a = words[j] & 0x7fff7fffu;
+    uint32_t v;
+    asm("fma.rn.relu.bf16x2 %0, %1, %2, %3;" : "=r"(v) : "r"(a), "r"(one), "r"(nc));
+    if constexpr (GAMMA) {
+      uint32_t sq;
+      asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(sq) : "r"(v), "r"(v));
+      asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(acc) : "r"(sq), "r"(G2b[j]), "r"(acc));
+    } else {
+      asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(acc) : "r"(v), "r"(v), "r"(acc));
+    }
+  }
+  return __fadd_rn(bits_f32(acc << 16), bits_f32(acc & 0xffff0000u));
+}
+
+// The same sum in fp32 from the signed pairs t2 (f16 inputs).
+template <bool GAMMA>
+__device__ __forceinline__ float clip_excess_f32(const unsigned long long (&t2)[16], float c, const float* Gw) {
+  const unsigned long long C2 = pack2(c, c);
+  unsigned long long acc = 0ull;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const f2 v = unpack2(add2(t2[j] | 0x8000000080000000ull, C2));  // c - |t|: negative where clipped
+    const unsigned long long vv = pack2(fminf(v.x, 0.0f), fminf(v.y, 0.0f));
+    if constexpr (GAMMA) {
+      acc = fma2(mul2(vv, vv), load_g2(Gw, j), acc);
+    } else {
+      acc = fma2(vv, vv, acc);
+    }
+  }
+  const f2 r = unpack2(acc);
+  return __fadd_rn(r.x, r.y);
+}
+
+// Exact error of candidate e for one block, the warp cooperating: `a` is |t|
+// of element `lane` of the block and `g2` its gamma^2.  Every operation is the
+// one candidate_error<GAMMA, false> performs for that element, and the
+// shuffles rebuild its order: lane partials ((x_l + x_l+8) + x_l+16) + x_l+24,
+// then p_0 + ... + p_7 left to right.  Returns the error to every lane.
+template <bool GAMMA>
+__device__ __forceinline__ float coop_error(float a, float g2, int e) {
+  const float x = __fmul_rn(a, exp2i(-e));
+  uint32_t h2;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(h2) : "f"(0.0f), "f"(x));
+  const float q = __low2float(*reinterpret_cast<const __half2*>(&h2));
+  const float d = __fmaf_rn(q, exp2i(e), -a);
+  float sq = __fmul_rn(d, d);
+  if constexpr (GAMMA) sq = __fmul_rn(sq, g2);
+  float v = __fadd_rn(sq, __shfl_down_sync(0xffffffffu, sq, 8));
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, sq, 16));
+  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, sq, 24));
+  float acc = __shfl_sync(0xffffffffu, v, 0);
+#pragma unroll
+  for (int k = 1; k < 8; ++k) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, k));
+  return __fmul_rn(acc, 0.03125f);
+}
+
+// |t| of element `lane` of the block in tile row `row`, block column w, from
+// the 128B-swizzled stage (the layout stage_words reads).
+template <int DT>
+__device__ __forceinline__ float stage_magnitude(const uint8_t* stage, int w, int row, int lane) {
+  const uint8_t* p = stage + (w >> 1) * kBoxBytes + row * 128 +
+                     ((((4 * (w & 1)) + (lane >> 3)) ^ (row & 7)) << 4) + ((lane & 7) << 1);
+  const uint32_t h = *reinterpret_cast<const uint16_t*>(p);
+  if constexpr (DT == MXW_BF16) return bits_f32((h & 0x7fffu) << 16);
+  return fabsf(__half2float(__ushort_as_half(static_cast<unsigned short>(h))));
+}
+
+// E2M1 round trip of four signed pairs: the values as f16x2 words and the
+// four code bytes packed into one word (pair k in byte k, element 2j in the
+// low nibble of its byte).
+__device__ __forceinline__ uint32_t e2m1_quad(const unsigned long long (&x)[4], uint32_t (&h)[4]) {
+  const f2 a = unpack2(x[0]), b = unpack2(x[1]), c = unpack2(x[2]), d = unpack2(x[3]);
+  uint32_t codes;
+  asm("{\n\t.reg .b8 t0, t1, t2, t3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t0, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t1, %8, %7;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t2, %10, %9;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t3, %12, %11;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, t0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, t1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, t2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, t3;\n\t"
+      "mov.b32 %4, {t0, t1, t2, t3};\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3]), "=r"(codes)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y), "f"(d.x), "f"(d.y));
+  return codes;
+}
+
+__device__ __forceinline__ unsigned long long f16x2_to_f32x2(uint32_t h) {
+  const __half2 hh = *reinterpret_cast<const __half2*>(&h);
+  return pack2(__low2float(hh), __high2float(hh));
+}
+
+// Errors of candidates f and f+1 in one pass over the block's signed pairs,
+// with each candidate's packed codes.  Per element and candidate, in the
+// reference's rounding: x = t / 2^e (exact here: |t| >= 2^-133 and e <= 15,
+// so nothing underflows; +0 is added to turn -0 into +0 as the reference's
+// sign rule does), q = E2M1(x) by hardware RNE with saturation,
+// dW = fl(q*2^e - t) (computed as fl(t - q*2^e), the same magnitude),
+// fl(dW^2), fl(. * gamma^2), then the lane partials and their left-to-right
+// sum, / 32.  The codes of x are the final encode's codes when e wins
+// (core.py:242-249 recomputes the same x).
+template <bool GAMMA>
+__device__ __forceinline__ void two_candidate_errors(const unsigned long long (&t2)[16], int f, const float* Gw,
+                                                     const QuantParams& P, float& e0, float& e1, uint4& pk0,
+                                                     uint4& pk1) {
+  const unsigned long long Z2 = pack2(P.zero, P.zero);
+  const unsigned long long NZ2 = pack2(P.negzero, P.negzero);
+  const float i0 = exp2i(-f), s0 = -exp2i(f);
+  const unsigned long long I0 = pack2(i0, i0), I1 = pack2(0.5f * i0, 0.5f * i0);
+  const unsigned long long S0 = pack2(s0, s0), S1 = pack2(2.0f * s0, 2.0f * s0);
+  unsigned long long p0[4], p1[4];
+  uint32_t w0[4], w1[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    unsigned long long xa[4], xb[4];
+    uint32_t ha[4], hb[4];
+#pragma unroll
+    for (int lp = 0; lp < 4; ++lp) {
+      xa[lp] = fma2(t2[q * 4 + lp], I0, Z2);
+      xb[lp] = fma2(t2[q * 4 + lp], I1, Z2);
+    }
+    w0[q] = e2m1_quad(xa, ha);
+    w1[q] = e2m1_quad(xb, hb);
+#pragma unroll
+    for (int lp = 0; lp < 4; ++lp) {
+      const int j = q * 4 + lp;
+      const unsigned long long da = fma2(f16x2_to_f32x2(ha[lp]), S0, t2[j]);
+      const unsigned long long db = fma2(f16x2_to_f32x2(hb[lp]), S1, t2[j]);
+      unsigned long long sa = mul2_rounded(da, da, NZ2);
+      unsigned long long sb = mul2_rounded(db, db, NZ2);
+      if constexpr (GAMMA) {
+        const unsigned long long g = load_g2(Gw, j);
+        sa = mul2_rounded(sa, g, NZ2);
+        sb = mul2_rounded(sb, g, NZ2);
+      }
+      p0[lp] = (q == 0) ? sa : add2(p0[lp], sa);
+      p1[lp] = (q == 0) ? sb : add2(p1[lp], sb);
+    }
+  }
+  float a0 = __fadd_rn(unpack2(p0[0]).x, unpack2(p0[0]).y);
+  float a1 = __fadd_rn(unpack2(p1[0]).x, unpack2(p1[0]).y);
+#pragma unroll
+  for (int lp = 1; lp < 4; ++lp) {
+    a0 = __fadd_rn(__fadd_rn(a0, unpack2(p0[lp]).x), unpack2(p0[lp]).y);
+    a1 = __fadd_rn(__fadd_rn(a1, unpack2(p1[lp]).x), unpack2(p1[lp]).y);
+  }
+  e0 = __fmul_rn(a0, 0.03125f);
+  e1 = __fmul_rn(a1, 0.03125f);
+  pk0 = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+  pk1 = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+}
+
+// Warp-collective: every lane calls it; `active` marks lanes whose tile row
+// exists.  Reads its block (tile row `lane`, block column w) from the stage,
+// which the caller keeps until this returns.  Returns the E8M0 byte (or
+// kRareBlock) and the packed codes; `nonfinite` reports NaN/inf in the block.
+template <int DT, int OBJ, int QM>
+__device__ __forceinline__ uint32_t quantize_block_fast(bool active, const QuantParams& P, const uint8_t* stage,
+                                                        int w, int lane, const float* Gw, const uint32_t* G2b,
+                                                        float g2_lane, uint4& packed, bool& nonfinite) {
+  constexpr bool GAMMA = OBJ == kObjGamma;
+  float amax, second;
+  unsigned long long t2[16];
+  {
+    uint32_t words[16];
+    stage_words(stage, w, lane, words);
+    // Magnitude order statistics on the raw 16-bit patterns (sign-magnitude:
+    // the integer order is the order of |value|; NaN/inf on top).
+    uint32_t m1 = 0, m2 = 0;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const uint32_t a = words[k] & 0x7fff7fffu;
+      if constexpr (QM == kQTop2) m2 = __vmaxu2(m2, __vminu2(m1, a));
+      m1 = __vmaxu2(m1, a);
+      t2[k] = word_pair<DT>(words[k]);
+    }
+    const uint32_t lo1 = m1 & 0xffffu, hi1 = m1 >> 16;
+    const uint32_t top1 = max(lo1, hi1);
+    uint32_t top2 = 0;
+    if constexpr (QM == kQTop2) top2 = max(min(lo1, hi1), max(m2 & 0xffffu, m2 >> 16));
+    if constexpr (DT == MXW_BF16) {
+      nonfinite = top1 >= 0x7f80u;
+      amax = bits_f32(top1 << 16);
+      second = bits_f32(top2 << 16);
+    } else {
+      nonfinite = top1 >= 0x7c00u;
+      amax = __half2float(__ushort_as_half(static_cast<unsigned short>(top1)));
+      second = __half2float(__ushort_as_half(static_cast<unsigned short>(top2)));
+    }
+  }
+  unsigned long long unused_nt2[16];
+  const float anchor = fmaxf(block_anchor<QM>(amax, second, unused_nt2, P), 1e-6f);
+  const bool near_zero = amax < 1e-6f;
+  bool fast = active && !near_zero && !nonfinite;
+  const int f = fast ? floor_log2_div6(anchor) : 0;
+  const int safe_e = fast ? ceil_log2_div6(fmaxf(amax, 1e-12f)) : 0;
+  // f >= -23 (the anchor is at least 1e-6), so f - depth is never clamped;
+  // f <= 14 keeps t / 2^e exact for the codes of f and f+1.
+  fast = fast && f <= 14 && safe_e <= f + 2;
+
+  float e_f, e_f1;
+  uint4 pk_f, pk_f1;
+  two_candidate_errors<GAMMA>(t2, f, Gw, P, e_f, e_f1, pk_f, pk_f1);
+  fast = fast && !isnan(e_f) && !isnan(e_f1);
+  const float e_hi = fminf(e_f, e_f1);
+
+  // Clipping candidates below f: certified losers, or evaluated below.
+  bool need_low = fast && P.depth > 0;
+  if (__any_sync(0xffffffffu, need_low)) {
+    const float c = __fmul_rn(exp2i(f), 3.0f);  // 6 * 2^(f-1), exact
+    if constexpr (!GAMMA) {
+      const float v1 = fmaxf(__fsub_rn(amax, c), 0.0f);
+      const float v2 = QM == kQTop2 ? fmaxf(__fsub_rn(second, c), 0.0f) : 0.0f;
+      const float lb = __fmul_rn(__fadd_rn(__fmul_rn(v1, v1), __fmul_rn(v2, v2)), 0.03125f);
+      need_low = need_low && !lb_prunes(lb, e_hi);
+    }
+    if (__any_sync(0xffffffffu, need_low)) {
+      float sum;
+      if constexpr (DT == MXW_BF16) {
+        uint32_t wd[16];
+        stage_words(stage, w, lane, wd);
+        sum = clip_excess_bf16<GAMMA>(wd, c, G2b);
+      } else {
+        sum = clip_excess_f32<GAMMA>(t2, c, Gw);
+      }
+      need_low = need_low && !lb_prunes(__fmul_rn(sum, 0.03125f), e_hi);
+    }
+  }
+  const bool need_safe = fast && safe_e == f + 2;
+  const int lo_e = f - P.depth;
+
+  // Argmin in the reference's order (core.py:220-238): strict <, the first
+  // candidate is the initial choice, NaN propagates through the minimum.
+  int raw = lo_e;
+  float best = __int_as_float(0x7f800000);
+  uint32_t m = __ballot_sync(0xffffffffu, need_low);
+  while (m) {
+    const int src = __ffs(m) - 1;
+    m &= m - 1;
+    const float a = stage_magnitude<DT>(stage, w, src, lane);
+    const int c0 = __shfl_sync(0xffffffffu, lo_e, src), c1 = __shfl_sync(0xffffffffu, f, src);
+    for (int c = c0; c < c1; ++c) {
+      const float err = coop_error<GAMMA>(a, g2_lane, c);
+      if (lane == src) {
+        if (err < best) raw = c;
+        best = nan_min(best, err);
+      }
+    }
+  }
+  if (e_f < best) raw = f;
+  best = nan_min(best, e_f);
+  if (e_f1 < best) raw = f + 1;
+  best = nan_min(best, e_f1);
+  m = __ballot_sync(0xffffffffu, need_safe);
+  while (m) {
+    const int src = __ffs(m) - 1;
+    m &= m - 1;
+    const float a = stage_magnitude<DT>(stage, w, src, lane);
+    const float err = coop_error<GAMMA>(a, g2_lane, __shfl_sync(0xffffffffu, safe_e, src));
+    if (lane == src && err < best) raw = safe_e;
+  }
+
+  if (near_zero && active && !nonfinite) {
+    // t is replaced by zeros (core.py:194-195): the first candidate wins,
+    // with f from the clamped anchor 1e-6.
+    packed = make_uint4(0u, 0u, 0u, 0u);
+    return static_cast<uint32_t>(floor_log2_div6(anchor) - P.depth + 127);
+  }
+  if (!fast) return kRareBlock;
+  if (raw == f) {
+    packed = pk_f;
+  } else if (raw == f + 1) {
+    packed = pk_f1;
+  } else {
+    // A candidate the warp evaluated won: encode it from the stage.
+    uint32_t wd[16];
+    stage_words(stage, w, lane, wd);
+    encode_pairs([&](int j) { return word_pair<DT>(wd[j]); }, P, raw, packed);
+  }
+  return static_cast<uint32_t>(raw + 127);
+}
+
 // --------------------------------------------------------------- TMA kernel
+
+// (strip, row tile) of consecutive strip-major tiles: one 64-bit division per
+// CTA instead of one per tile.
+struct TileCursor {
+  int64_t strip, rt;
+  __device__ __forceinline__ TileCursor(int64_t t, int64_t n_row_tiles) : strip(t / n_row_tiles), rt(t % n_row_tiles) {}
+  __device__ __forceinline__ void advance(int64_t n_row_tiles) {
+    if (++rt == n_row_tiles) {
+      rt = 0;
+      ++strip;
+    }
+  }
+};
 
 template <int DT, int OBJ, int QM>
 __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F32) ? 1 : 2)
@@ -499,7 +910,7 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   float* Hs = reinterpret_cast<float*>(scale_stage + kOutBuffers * kScaleTileBytes);
   float* Gs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(Hs) + (OBJ == kObjHess ? kTileBlocks * 1024 * 4 : 0));
   uint64_t* full =
-      reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(Gs) + (OBJ == kObjGamma ? kTileBlocks * kBlock * 4 : 0));
+      reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(Gs) + (OBJ == kObjGamma ? kTileBlocks * kGammaWords * 4 : 0));
   uint64_t* empty = full + kStages;
   uint64_t* out_full = empty + kStages;
   uint64_t* out_empty = out_full + kOutBuffers;
@@ -528,8 +939,9 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
     bool ok = true;
     int64_t it = 0;
     const bool scale_words = (P.nb % 8 == 0) && (reinterpret_cast<uintptr_t>(P.scales) % 8 == 0);
-    for (int64_t t = t_begin; t < t_end; ++t, ++it) {
-      const int64_t strip = t / P.n_row_tiles, rt = t % P.n_row_tiles;
+    TileCursor cur(t_begin, P.n_row_tiles);
+    for (int64_t t = t_begin; t < t_end; ++t, ++it, cur.advance(P.n_row_tiles)) {
+      const int64_t strip = cur.strip, rt = cur.rt;
       const int buf = static_cast<int>(it % kOutBuffers);
       if (!__all_sync(0xffffffffu, mbar_wait(&out_full[buf], static_cast<uint32_t>((it / kOutBuffers) & 1)))) {
         ok = false;
@@ -571,8 +983,9 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       prefetch_tensormap(&map);
       int64_t issued = 0;
       bool ok = true;
-      for (int64_t t = t_begin; t < t_end; ++t, ++issued) {
-        const int64_t strip = t / P.n_row_tiles, rt = t % P.n_row_tiles;
+      TileCursor cur(t_begin, P.n_row_tiles);
+      for (int64_t t = t_begin; t < t_end; ++t, ++issued, cur.advance(P.n_row_tiles)) {
+        const int64_t strip = cur.strip, rt = cur.rt;
         const int64_t col0 = strip * kTileBlocks * kBlock;
         const int64_t left = (P.cols - col0 + Elem<DT>::kBoxCols - 1) / Elem<DT>::kBoxCols;
         const int boxes = left < Elem<DT>::kBoxesPerStage ? static_cast<int>(left) : Elem<DT>::kBoxesPerStage;
@@ -598,19 +1011,24 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   // ---------------- consumer warps: warp w owns block column strip*8 + w.
   unsigned long long g2[16];  // unused here: gamma^2 lives in shared memory (Gw)
   float* Hw = Hs + warp * 1024;
-  float* Gw = Gs + warp * kBlock;
+  float* Gw = Gs + warp * kGammaWords;
+  float g2_lane = 0.0f;  // gamma^2 of column element `lane` (the fast path's warp evaluation)
   int64_t cur_strip = -1;
   bool valid_col = false;
   int64_t b = 0;
   bool any_nonfinite = false;
   int64_t it = 0;
-  for (int64_t t = t_begin; t < t_end; ++t, ++it) {
-    const int64_t strip = t / P.n_row_tiles, rt = t % P.n_row_tiles;
+  TileCursor cur(t_begin, P.n_row_tiles);
+  for (int64_t t = t_begin; t < t_end; ++t, ++it, cur.advance(P.n_row_tiles)) {
+    const int64_t strip = cur.strip, rt = cur.rt;
     if (strip != cur_strip) {
       cur_strip = strip;
       b = strip * kTileBlocks + warp;
       valid_col = b < P.nb;
-      if (valid_col) load_column_state<OBJ>(P, b, lane, Hw, Gw);
+      if (valid_col) {
+        load_column_state<OBJ>(P, b, lane, Hw, Gw);
+        if constexpr (OBJ == kObjGamma) g2_lane = Gw[lane];
+      }
     }
     const int s = static_cast<int>(it % kStages);
     // Warp-uniform verdict: a lane that timed out takes the whole warp out.
@@ -624,13 +1042,24 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
     uint4 pk = make_uint4(0u, 0u, 0u, 0u);
     uint32_t sc = 0;
     if (valid_col) {
-      BlockData<DT> B;
-      read_block_smem<DT, QM>(stages + s * kStageBytes, warp, lane, B);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (rt * kTileRows + lane < P.rows) {
-        any_nonfinite |= B.nonfinite;
-        sc = quantize_one_block<DT, OBJ, QM, true, true, OBJ != kObjHess>(B, P, g2, Hw, pk, Gw);
+      const bool active = rt * kTileRows + lane < P.rows;
+      if constexpr (FastPath<DT, OBJ, QM>::value) {
+        // Warp-collective; the stage stays held until its warp evaluation is done.
+        bool nf = false;
+        sc = quantize_block_fast<DT, OBJ, QM>(active, P, stages + s * kStageBytes, warp, lane, Gw,
+                                              reinterpret_cast<const uint32_t*>(Gw + kBlock), g2_lane, pk, nf);
+        any_nonfinite |= active && nf;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      } else {
+        BlockData<DT> B;
+        read_block_smem<DT, QM>(stages + s * kStageBytes, warp, lane, B);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (active) {
+          any_nonfinite |= B.nonfinite;
+          sc = quantize_one_block<DT, OBJ, QM, true, true, OBJ != kObjHess>(B, P, g2, Hw, pk, Gw);
+        }
       }
     } else {
       __syncwarp();
@@ -817,7 +1246,7 @@ static LaunchInfo& launch_info(const void* kern, int dev) {
 template <int DT, int OBJ, int QM>
 static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStream_t stream) {
   const size_t smem = 1024 + kStages * Elem<DT>::kStageBytes + kOutBuffers * (kOutTileBytes + kScaleTileBytes) +
-                      (OBJ == kObjHess ? kTileBlocks * 4096 : 0) + (OBJ == kObjGamma ? kTileBlocks * kBlock * 4 : 0) +
+                      (OBJ == kObjHess ? kTileBlocks * 4096 : 0) + (OBJ == kObjGamma ? kTileBlocks * kGammaWords * 4 : 0) +
                       (2 * kStages + 2 * kOutBuffers) * sizeof(uint64_t);
   CUtensorMap map;
   const CUtensorMapDataType dt = DT == MXW_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16

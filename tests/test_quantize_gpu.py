@@ -305,3 +305,27 @@ def test_near_flt_max_blocks_in_a_large_tensor(objective, depth, cuda_device) ->
     block_max = np.abs(syn.bf16_bits_to_f32(bits)).reshape(rows, cols // 32, 32).max(axis=-1)
     assert (block_max > 6.0 * 2.0 ** 125).any(), "the case must contain blocks with e >= 126 candidates"
     assert_same_bytes(bits, p, s, po, so)
+
+
+@pytest.mark.parametrize("pct", [99.5, 97.0, 100.0])
+@pytest.mark.parametrize("depth", [0, 1, 2, 4, 8])
+@pytest.mark.parametrize("objective", ["none", "gamma"])
+def test_close_call_blocks_match_oracle(objective, depth, pct, cuda_device) -> None:
+    """Inputs that push many blocks off the kernel's two-candidate fast path:
+    extreme per-channel gamma (clipping candidates below the anchor exponent
+    win or come close, so their lower bound does not decide and the warp
+    evaluates them exactly) and dense outliers (the no-clipping exponent is
+    two above the anchor's).  Bytes must match the oracle everywhere."""
+    rows, cols = 192, 2048
+    seed = 900 + 10 * depth + int(pct)
+    w = syn.det_dense_weight(rows, cols, seed, outlier_fraction=0.03)
+    kw: dict = {"mse_clip_depth": depth, "scale_percentile": pct}
+    okw = dict(kw)
+    if objective == "gamma":
+        z = syn.det_normal(cols, seed + 1)
+        g = np.exp(3.0 * z).astype(np.float32)  # channel weights over ~8 decades
+        g[::97] = 0.0
+        kw["gamma"], okw["gamma"] = torch.from_numpy(g).to(cuda_device), g
+    p, s = _gpu(_to_device(w, cuda_device), cuda_device, **kw)
+    po, so = oracle.quantize_mxfp4(w, **okw)
+    assert_same_bytes(w, p, s, po, so)
