@@ -14,6 +14,11 @@
 // exact f16x2 in the same asm block), two f16->f32 conversions, and packed
 // fp32 FMA / multiply / add.
 //
+// For 2-byte inputs with the unweighted or gamma objective and a top-2/amax
+// anchor, a fast path evaluates only the f and f+1 candidates per block and
+// rules out the rest with certified bounds (see quantize_block_fast); the
+// Hessian objective, fp32 inputs and low percentiles evaluate every candidate.
+//
 // Data layout: one thread owns one 32-element block.  A warp owns one block
 // column and 32 consecutive rows, so gamma and the block's 32x32 Hessian are
 // shared by the whole warp (registers / shared-memory broadcast).
@@ -561,18 +566,19 @@ __device__ __forceinline__ void load_column_state(const QuantParams& P, int64_t 
 // candidate's codes.  The clipping candidates below f are dropped when a lower
 // bound on the error of f-1 certifiably exceeds min(E_f, E_f+1): the bound
 // grows as the clip threshold falls, so it covers every deeper candidate too,
-// and a strictly larger error never wins the strict-< argmin.  The blocks the
-// bound does not decide, and the blocks whose safe exponent is f+2, get those
-// candidates evaluated exactly by the whole warp together: lane = element,
-// read from the tile still held in shared memory, with the reference's
-// summation order kept through shuffles.  Blocks outside the path's
+// and a strictly larger error never wins the strict-< argmin.  Only warps with
+// a block the bound does not decide (none unweighted on normal weights, about
+// a quarter with gamma weights), or with a block whose safe exponent is f+2,
+// evaluate those extra candidates, each thread for its own block.  Blocks
+// outside the path's
 // preconditions (non-finite values, block scales of 2^15 and above,
 // safe >= f+3, NaN errors) take the rare marker and are finished by
 // quantize_fixup_kernel.
 
 template <int DT, int OBJ, int QM>
 struct FastPath {
-  static constexpr bool value = Elem<DT>::kBytes == 2 && OBJ == kObjNone && (QM == kQTop2 || QM == kQAmax);
+  static constexpr bool value =
+      Elem<DT>::kBytes == 2 && (OBJ == kObjNone || OBJ == kObjGamma) && (QM == kQTop2 || QM == kQAmax);
 };
 
 __device__ __forceinline__ float nan_min(float best, float err) {
@@ -629,41 +635,6 @@ __device__ __forceinline__ float clip_excess_f32(const unsigned long long (&t2)[
   }
   const f2 r = unpack2(acc);
   return __fadd_rn(r.x, r.y);
-}
-
-// Exact error of candidate e for one block, the warp cooperating: `a` is |t|
-// of element `lane` of the block and `g2` its gamma^2.  Every operation is the
-// one candidate_error<GAMMA, false> performs for that element, and the
-// shuffles rebuild its order: lane partials ((x_l + x_l+8) + x_l+16) + x_l+24,
-// then p_0 + ... + p_7 left to right.  Returns the error to every lane.
-template <bool GAMMA>
-__device__ __forceinline__ float coop_error(float a, float g2, int e) {
-  const float x = __fmul_rn(a, exp2i(-e));
-  uint32_t h2;
-  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
-      : "=r"(h2) : "f"(0.0f), "f"(x));
-  const float q = __low2float(*reinterpret_cast<const __half2*>(&h2));
-  const float d = __fmaf_rn(q, exp2i(e), -a);
-  float sq = __fmul_rn(d, d);
-  if constexpr (GAMMA) sq = __fmul_rn(sq, g2);
-  float v = __fadd_rn(sq, __shfl_down_sync(0xffffffffu, sq, 8));
-  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, sq, 16));
-  v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, sq, 24));
-  float acc = __shfl_sync(0xffffffffu, v, 0);
-#pragma unroll
-  for (int k = 1; k < 8; ++k) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, k));
-  return __fmul_rn(acc, 0.03125f);
-}
-
-// |t| of element `lane` of the block in tile row `row`, block column w, from
-// the 128B-swizzled stage (the layout stage_words reads).
-template <int DT>
-__device__ __forceinline__ float stage_magnitude(const uint8_t* stage, int w, int row, int lane) {
-  const uint8_t* p = stage + (w >> 1) * kBoxBytes + row * 128 +
-                     ((((4 * (w & 1)) + (lane >> 3)) ^ (row & 7)) << 4) + ((lane & 7) << 1);
-  const uint32_t h = *reinterpret_cast<const uint16_t*>(p);
-  if constexpr (DT == MXW_BF16) return bits_f32((h & 0x7fffu) << 16);
-  return fabsf(__half2float(__ushort_as_half(static_cast<unsigned short>(h))));
 }
 
 // E2M1 round trip of four signed pairs: the values as f16x2 words and the
@@ -752,14 +723,47 @@ __device__ __forceinline__ void two_candidate_errors(const unsigned long long (&
   pk1 = make_uint4(w1[0], w1[1], w1[2], w1[3]);
 }
 
-// Warp-collective: every lane calls it; `active` marks lanes whose tile row
-// exists.  Reads its block (tile row `lane`, block column w) from the stage,
-// which the caller keeps until this returns.  Returns the E8M0 byte (or
-// kRareBlock) and the packed codes; `nonfinite` reports NaN/inf in the block.
+// Error of one candidate e from the signed pairs: the arithmetic of
+// two_candidate_errors without the codes.  t / 2^e is exact for the exponents
+// the fast path evaluates here (f - 8 <= e <= f + 2 <= 16).
+template <bool GAMMA>
+__device__ __forceinline__ float one_candidate_error(const unsigned long long (&t2)[16], int e, const float* Gw,
+                                                     const QuantParams& P) {
+  const unsigned long long Z2 = pack2(P.zero, P.zero);
+  const unsigned long long NZ2 = pack2(P.negzero, P.negzero);
+  const float i = exp2i(-e), sc = -exp2i(e);
+  const unsigned long long I2 = pack2(i, i), S2 = pack2(sc, sc);
+  unsigned long long p[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int lp = 0; lp < 4; ++lp) {
+      const int j = q * 4 + lp;
+      const f2 x = unpack2(fma2(t2[j], I2, Z2));
+      uint32_t h2;
+      asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+          : "=r"(h2) : "f"(x.y), "f"(x.x));
+      const unsigned long long d = fma2(f16x2_to_f32x2(h2), S2, t2[j]);
+      unsigned long long sq = mul2_rounded(d, d, NZ2);
+      if constexpr (GAMMA) sq = mul2_rounded(sq, load_g2(Gw, j), NZ2);
+      p[lp] = (q == 0) ? sq : add2(p[lp], sq);
+    }
+  }
+  float acc = __fadd_rn(unpack2(p[0]).x, unpack2(p[0]).y);
+#pragma unroll
+  for (int lp = 1; lp < 4; ++lp) acc = __fadd_rn(__fadd_rn(acc, unpack2(p[lp]).x), unpack2(p[lp]).y);
+  return __fmul_rn(acc, 0.03125f);
+}
+
+// Warp-collective (the extra candidates run under warp votes): every lane
+// calls it; `active` marks lanes whose tile row exists.  Reads its block (tile
+// row `lane`, block column w) from the stage; lane 0 releases the stage on
+// `release` once the warp has read it.  Returns the E8M0 byte (or
+// kRareBlock) and the packed codes; `nonfinite` reports NaN/inf.
 template <int DT, int OBJ, int QM>
 __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const QuantParams& P, const uint8_t* stage,
                                                         int w, int lane, const float* Gw, const uint32_t* G2b,
-                                                        float g2_lane, uint4& packed, bool& nonfinite) {
+                                                        uint64_t* release, uint4& packed, bool& nonfinite) {
   constexpr bool GAMMA = OBJ == kObjGamma;
   float amax, second;
   unsigned long long t2[16];
@@ -790,6 +794,8 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
       second = __half2float(__ushort_as_half(static_cast<unsigned short>(top2)));
     }
   }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(release);
   unsigned long long unused_nt2[16];
   const float anchor = fmaxf(block_anchor<QM>(amax, second, unused_nt2, P), 1e-6f);
   const bool near_zero = amax < 1e-6f;
@@ -819,8 +825,10 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
     if (__any_sync(0xffffffffu, need_low)) {
       float sum;
       if constexpr (DT == MXW_BF16) {
-        uint32_t wd[16];
-        stage_words(stage, w, lane, wd);
+        uint32_t wd[16];  // the bf16 words again, from the exact fp32 pairs
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          wd[j] = __byte_perm(static_cast<uint32_t>(t2[j]), static_cast<uint32_t>(t2[j] >> 32), 0x7632);
         sum = clip_excess_bf16<GAMMA>(wd, c, G2b);
       } else {
         sum = clip_excess_f32<GAMMA>(t2, c, Gw);
@@ -835,16 +843,11 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
   // candidate is the initial choice, NaN propagates through the minimum.
   int raw = lo_e;
   float best = __int_as_float(0x7f800000);
-  uint32_t m = __ballot_sync(0xffffffffu, need_low);
-  while (m) {
-    const int src = __ffs(m) - 1;
-    m &= m - 1;
-    const float a = stage_magnitude<DT>(stage, w, src, lane);
-    const int c0 = __shfl_sync(0xffffffffu, lo_e, src), c1 = __shfl_sync(0xffffffffu, f, src);
-    for (int c = c0; c < c1; ++c) {
-      const float err = coop_error<GAMMA>(a, g2_lane, c);
-      if (lane == src) {
-        if (err < best) raw = c;
+  if (__any_sync(0xffffffffu, need_low)) {
+    for (int k = 0; k < P.depth; ++k) {
+      const float err = one_candidate_error<GAMMA>(t2, lo_e + k, Gw, P);
+      if (need_low) {
+        if (err < best) raw = lo_e + k;
         best = nan_min(best, err);
       }
     }
@@ -853,13 +856,9 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
   best = nan_min(best, e_f);
   if (e_f1 < best) raw = f + 1;
   best = nan_min(best, e_f1);
-  m = __ballot_sync(0xffffffffu, need_safe);
-  while (m) {
-    const int src = __ffs(m) - 1;
-    m &= m - 1;
-    const float a = stage_magnitude<DT>(stage, w, src, lane);
-    const float err = coop_error<GAMMA>(a, g2_lane, __shfl_sync(0xffffffffu, safe_e, src));
-    if (lane == src && err < best) raw = safe_e;
+  if (__any_sync(0xffffffffu, need_safe)) {
+    const float err = one_candidate_error<GAMMA>(t2, safe_e, Gw, P);
+    if (need_safe && err < best) raw = safe_e;
   }
 
   if (near_zero && active && !nonfinite) {
@@ -874,10 +873,7 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
   } else if (raw == f + 1) {
     packed = pk_f1;
   } else {
-    // A candidate the warp evaluated won: encode it from the stage.
-    uint32_t wd[16];
-    stage_words(stage, w, lane, wd);
-    encode_pairs([&](int j) { return word_pair<DT>(wd[j]); }, P, raw, packed);
+    encode_pairs([&](int j) { return t2[j]; }, P, raw, packed);  // an extra candidate won
   }
   return static_cast<uint32_t>(raw + 127);
 }
@@ -1012,7 +1008,6 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   unsigned long long g2[16];  // unused here: gamma^2 lives in shared memory (Gw)
   float* Hw = Hs + warp * 1024;
   float* Gw = Gs + warp * kGammaWords;
-  float g2_lane = 0.0f;  // gamma^2 of column element `lane` (the fast path's warp evaluation)
   int64_t cur_strip = -1;
   bool valid_col = false;
   int64_t b = 0;
@@ -1025,10 +1020,7 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       cur_strip = strip;
       b = strip * kTileBlocks + warp;
       valid_col = b < P.nb;
-      if (valid_col) {
-        load_column_state<OBJ>(P, b, lane, Hw, Gw);
-        if constexpr (OBJ == kObjGamma) g2_lane = Gw[lane];
-      }
+      if (valid_col) load_column_state<OBJ>(P, b, lane, Hw, Gw);
     }
     const int s = static_cast<int>(it % kStages);
     // Warp-uniform verdict: a lane that timed out takes the whole warp out.
@@ -1045,12 +1037,11 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       const bool active = rt * kTileRows + lane < P.rows;
       if constexpr (FastPath<DT, OBJ, QM>::value) {
         // Warp-collective; the stage stays held until its warp evaluation is done.
+        // Warp-collective; it releases the stage once the warp has read it.
         bool nf = false;
         sc = quantize_block_fast<DT, OBJ, QM>(active, P, stages + s * kStageBytes, warp, lane, Gw,
-                                              reinterpret_cast<const uint32_t*>(Gw + kBlock), g2_lane, pk, nf);
+                                              reinterpret_cast<const uint32_t*>(Gw + kBlock), &empty[s], pk, nf);
         any_nonfinite |= active && nf;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
       } else {
         BlockData<DT> B;
         read_block_smem<DT, QM>(stages + s * kStageBytes, warp, lane, B);
