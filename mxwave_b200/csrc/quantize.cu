@@ -637,6 +637,12 @@ __device__ __forceinline__ float clip_excess_f32(const unsigned long long (&t2)[
   return __fadd_rn(r.x, r.y);
 }
 
+// gamma^2 pairs 4q .. 4q+3 of the warp's block column (two broadcast loads).
+__device__ __forceinline__ void load_g2_quad(const float* Gw, int q, unsigned long long (&g)[4]) {
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(g[0]), "=l"(g[1]) : "r"(smem_u32(Gw + 8 * q)));
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(g[2]), "=l"(g[3]) : "r"(smem_u32(Gw + 8 * q + 4)));
+}
+
 // E2M1 round trip of four signed pairs: the values as f16x2 words and the
 // four code bytes packed into one word (pair k in byte k, element 2j in the
 // low nibble of its byte).
@@ -685,8 +691,9 @@ __device__ __forceinline__ void two_candidate_errors(const unsigned long long (&
   uint32_t w0[4], w1[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    unsigned long long xa[4], xb[4];
+    unsigned long long xa[4], xb[4], g[4];
     uint32_t ha[4], hb[4];
+    if constexpr (GAMMA) load_g2_quad(Gw, q, g);  // issued early: its latency hides behind the conversions
 #pragma unroll
     for (int lp = 0; lp < 4; ++lp) {
       xa[lp] = fma2(t2[q * 4 + lp], I0, Z2);
@@ -702,9 +709,8 @@ __device__ __forceinline__ void two_candidate_errors(const unsigned long long (&
       unsigned long long sa = mul2_rounded(da, da, NZ2);
       unsigned long long sb = mul2_rounded(db, db, NZ2);
       if constexpr (GAMMA) {
-        const unsigned long long g = load_g2(Gw, j);
-        sa = mul2_rounded(sa, g, NZ2);
-        sb = mul2_rounded(sb, g, NZ2);
+        sa = mul2_rounded(sa, g[lp], NZ2);
+        sb = mul2_rounded(sb, g[lp], NZ2);
       }
       p0[lp] = (q == 0) ? sa : add2(p0[lp], sa);
       p1[lp] = (q == 0) ? sb : add2(p1[lp], sb);
