@@ -368,20 +368,27 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, k_ms = float(t[0]), float(t[1])
     peak = _peaks_tensor()
-    flops = 2.0 * (hi - lo) * k * k
+    # The Gram is symmetric: its k(k+1)/2 distinct entries take 2 flops per
+    # token each.  The kernel runs the 128 x 256 tiles that reach the upper
+    # triangle (row tile by holds column tiles by/2 ..); mma_flops counts them.
+    n = hi - lo
+    flops = 1.0 * n * k * (k + 1)
+    tiles = sum((k + 255) // 256 - (by >> 1) for by in range(k // 128))
+    mma_flops = 2.0 * n * 128 * 256 * tiles
     achieved = flops / (k_ms * 1e-3) / 1e12
     return {
         "metric": "calib tokens/s for X^T X",
         "value": round(total_tokens * args.steps / (ms * 1e-3), 1),
         "unit": "tokens/s",
         "scaling": "strong",
-        "config": {"workload": f"full X^T X of {total_tokens} x {k} bf16 activations -> fp32 Gram, "
+        "config": {"workload": f"full (symmetric) X^T X of {total_tokens} x {k} bf16 activations -> fp32 Gram, "
                                f"tokens split over {world} GPU(s), NCCL all-reduce of the Gram"},
         "ms_per_step": round(ms / args.steps, 4),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak[0], "unit": "TFLOP/s",
                      "frac": round(achieved / peak[0], 4), "peak_kind": peak[1], "kernel": "xtx_kernel (tcgen05)",
                      "traffic": XTX_TRAFFIC_BYTES if world == 1 else None, "traffic_unit": "bytes per launch (ncu)",
-                     "flops_per_launch": flops, "avg_launch_ms": round(k_ms, 4)},
+                     "flops_per_launch": flops, "mma_flops_per_launch": mma_flops,
+                     "mma_tflops": round(mma_flops / (k_ms * 1e-3) / 1e12, 1), "avg_launch_ms": round(k_ms, 4)},
         "gpu_launches": args.steps,
     }
 

@@ -11,6 +11,12 @@
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
 //               (kind::f16, bf16 x bf16 -> fp32, M=128 N=256 K=16, 4 per stage)
 //   warps 2..9  epilogue: each owns 32 TMEM lanes (rows) x 128 columns
+// Symmetry: G is symmetric, so only the tiles that reach the upper triangle
+// (column >= row somewhere in the tile) are computed -- 420 of 800 tiles at
+// 5120 channels.  A tile adds its entries with column >= row to G and the
+// transpose of those with column > row below the diagonal; for one column the
+// transposed entries are consecutive rows, so each warp's stores stay
+// coalesced.  Every entry of G is written by exactly one tile.
 // Accuracy: the tensor core's fp32 accumulation is not round-to-nearest (its
 // error grows with the number of K steps in one accumulator).  So tokens are
 // accumulated in chunks of 256 (16 K steps) in one of two TMEM buffers (2 x
@@ -46,6 +52,7 @@ constexpr int64_t kXtxMaxTokens = 262144;  // tokens per launch
 
 struct XtxParams {
   int64_t tokens, cols, ldg, n_kblocks;
+  int64_t n_col_tiles;  // 256-column tiles per row of tiles
   float* gram;
   uint32_t* flags;
 };
@@ -149,8 +156,17 @@ __global__ void __launch_bounds__(kXtxThreads, 1)
   int* fail = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t i0 = static_cast<int64_t>(blockIdx.y) * kXtxBM;
-  const int64_t j0 = static_cast<int64_t>(blockIdx.x) * kXtxBN;
+  // Tile blockIdx.x of the upper triangle, row by row: row tile `by` (128
+  // rows) holds the column tiles bx >= by / 2 (256 columns each), the first
+  // that reach column >= row.
+  int64_t by = 0, rem = blockIdx.x;
+  for (;; ++by) {
+    const int64_t in_row = P.n_col_tiles - (by >> 1);
+    if (rem < in_row) break;
+    rem -= in_row;
+  }
+  const int64_t i0 = by * kXtxBM;
+  const int64_t j0 = ((by >> 1) + rem) * kXtxBN;
   const int64_t n_chunks = (P.n_kblocks + kXtxChunkStages - 1) / kXtxChunkStages;
 
   if (threadIdx.x == 0) {
@@ -272,16 +288,36 @@ __global__ void __launch_bounds__(kXtxThreads, 1)
     if (!ok) atomicOr(fail, 1);
     // All epilogue warps agree before writing (named barrier 1, 256 threads).
     asm volatile("bar.sync 1, 256;" ::: "memory");
-    if (*reinterpret_cast<volatile int*>(fail) == 0 && j0 + 128 * half < P.cols) {
-      float* grow = P.gram + (i0 + 32 * quarter + lane) * P.ldg + j0 + 128 * half;
+    const int64_t r = i0 + 32 * quarter + lane;  // this thread's row of G
+    const int64_t cbase = j0 + 128 * half;        // its first column
+    if (*reinterpret_cast<volatile int*>(fail) == 0 && cbase < P.cols && cbase + 127 >= i0 + 32 * quarter) {
+      // Entries with column >= row, in place.
+      float* grow = P.gram + r * P.ldg + cbase;
 #pragma unroll
       for (int k = 0; k < 32; ++k) {
-        float4 o = reinterpret_cast<float4*>(grow)[k];
-        o.x = __fadd_rn(o.x, total[4 * k]);
-        o.y = __fadd_rn(o.y, total[4 * k + 1]);
-        o.z = __fadd_rn(o.z, total[4 * k + 2]);
-        o.w = __fadd_rn(o.w, total[4 * k + 3]);
-        reinterpret_cast<float4*>(grow)[k] = o;
+        const int64_t c = cbase + 4 * k;
+        if (c >= r) {
+          float4 o = reinterpret_cast<float4*>(grow)[k];
+          o.x = __fadd_rn(o.x, total[4 * k]);
+          o.y = __fadd_rn(o.y, total[4 * k + 1]);
+          o.z = __fadd_rn(o.z, total[4 * k + 2]);
+          o.w = __fadd_rn(o.w, total[4 * k + 3]);
+          reinterpret_cast<float4*>(grow)[k] = o;
+        } else if (c + 3 >= r) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (c + u >= r) grow[4 * k + u] = __fadd_rn(grow[4 * k + u], total[4 * k + u]);
+        }
+      }
+      // Their transposes below the diagonal: G[c, r] for c > r.  For one k
+      // the warp's 32 rows r are consecutive, so the stores coalesce.
+#pragma unroll
+      for (int k = 0; k < 128; ++k) {
+        const int64_t c = cbase + k;
+        if (c > r) {
+          float* g = P.gram + c * P.ldg + r;
+          *g = __fadd_rn(*g, total[k]);
+        }
       }
     }
   }
@@ -312,7 +348,12 @@ extern "C" int mxw_accumulate_xtx(const void* x, int64_t tokens, int64_t cols, i
   // One launch per slice of at most kXtxMaxTokens tokens: every on-device wait
   // stays far below the timeout, and each slice's TMEM accumulator is folded
   // into the fp32 Gram before the next one starts.
-  dim3 grid(static_cast<unsigned>((cols + kXtxBN - 1) / kXtxBN), static_cast<unsigned>(cols / kXtxBM));
+  // The tiles that reach the upper triangle: row tile by holds column tiles
+  // by/2 .. n_col_tiles-1.
+  const int64_t n_col_tiles = (cols + kXtxBN - 1) / kXtxBN;
+  int64_t n_tiles = 0;
+  for (int64_t by = 0; by < cols / kXtxBM; ++by) n_tiles += n_col_tiles - (by >> 1);
+  const dim3 grid(static_cast<unsigned>(n_tiles));
   for (int64_t t0 = 0; t0 < tokens; t0 += kXtxMaxTokens) {
     const int64_t n = std::min<int64_t>(kXtxMaxTokens, tokens - t0);
     CUtensorMap map;
@@ -324,6 +365,7 @@ extern "C" int mxw_accumulate_xtx(const void* x, int64_t tokens, int64_t cols, i
     P.cols = cols;
     P.ldg = ldg;
     P.n_kblocks = (n + kXtxBK - 1) / kXtxBK;
+    P.n_col_tiles = n_col_tiles;
     P.gram = gram;
     P.flags = flags;
     xtx_kernel<<<grid, kXtxThreads, smem, static_cast<cudaStream_t>(stream)>>>(map, P);

@@ -133,7 +133,7 @@ def _full_err(got: np.ndarray, ref: np.ndarray) -> float:
     return float(np.max(np.abs(got - ref) / scale))
 
 
-@pytest.mark.parametrize("tokens,cols", [(1, 128), (64, 128), (1000, 256), (4097, 640), (65536, 1024)])
+@pytest.mark.parametrize("tokens,cols", [(1, 128), (64, 128), (1000, 256), (300, 384), (4097, 640), (65536, 1024)])
 def test_xtx_matches_fp64(tokens, cols, cuda_device) -> None:
     lib = _lib.load()
     x, xf = _x(tokens, cols, tokens * 3 + cols, cuda_device)
@@ -142,7 +142,10 @@ def test_xtx_matches_fp64(tokens, cols, cuda_device) -> None:
     assert st == _lib.MXW_OK
     torch.cuda.synchronize()
     ref = oracle.gram(xf)
-    assert _full_err(g.cpu().numpy().astype(np.float64), ref) < RTOL
+    got = g.cpu().numpy()
+    assert _full_err(got.astype(np.float64), ref) < RTOL
+    # Only the upper triangle's tiles are computed; the lower one is their mirror.
+    assert np.array_equal(got, got.T)
 
 
 def test_xtx_accumulates_with_strides(cuda_device) -> None:
