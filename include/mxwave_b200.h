@@ -55,6 +55,7 @@ extern "C" {
 /* Bits of the device flag word written by the kernels. */
 #define MXW_FLAG_NONFINITE 1 /* the input held a NaN or infinity                 */
 #define MXW_FLAG_TIMEOUT 2   /* a bounded on-device wait gave up; output invalid */
+#define MXW_FLAG_RARE 4      /* quantize: a block took the exact rare-block pass  */
 
 /* Human-readable name of a status code. */
 MXW_API const char* mxw_status_string(int status);
@@ -77,6 +78,11 @@ MXW_API const char* mxw_version(void);
  *   gamma, hessian: device pointers or NULL (mutually exclusive; MSE only).
  *   flags: device uint32 word; MXW_FLAG_NONFINITE is OR-ed in when the slice
  *          holds a NaN or infinity (checkpoint.py:117), or NULL to skip.
+ *          MXW_FLAG_RARE is OR-ed in when some block needs the exact second
+ *          pass (non-finite values, magnitudes near FLT_MAX); with a flag word
+ *          whose MXW_FLAG_RARE bit is clear after the main pass, the second
+ *          pass returns at once instead of scanning the scale bytes.  The bit
+ *          is sticky: a word shared by several calls only costs extra scans.
  */
 MXW_API int mxw_quantize_mxfp4(const void* weight, int dtype, int64_t rows, int64_t cols, int64_t ld,
                        double scale_percentile, const float* gamma, const float* hessian,

@@ -31,6 +31,7 @@ MXW_DAMP_RELATIVE = 1
 
 MXW_FLAG_NONFINITE = 1
 MXW_FLAG_TIMEOUT = 2
+MXW_FLAG_RARE = 4
 
 _i64 = ctypes.c_int64
 _vp = ctypes.c_void_p

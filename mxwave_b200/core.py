@@ -161,11 +161,29 @@ def quantize_mxfp4(
             mse_clip_depth,
             packed.data_ptr(),
             scales.data_ptr(),
-            None if _flags is None else _flags.data_ptr(),
+            (_flags if _flags is not None else _device_flags(device)).data_ptr(),
             _stream_handle(device),
         )
     _lib.check(status, "mxw_quantize_mxfp4")
     return packed, scales
+
+
+_DEVICE_FLAGS: dict = {}
+
+
+def _device_flags(device: torch.device) -> torch.Tensor:
+    """A per-device flag word for calls that pass none.
+
+    Its MXW_FLAG_RARE bit lets the kernel skip the rare-block scan after a
+    main pass that marked nothing; the bits are sticky, so sharing the word
+    between calls and streams only costs extra scans.
+    """
+    key = (device.type, device.index)
+    flags = _DEVICE_FLAGS.get(key)
+    if flags is None:
+        flags = torch.zeros(1, dtype=torch.int32, device=device)
+        _DEVICE_FLAGS[key] = flags
+    return flags
 
 
 @torch.no_grad()

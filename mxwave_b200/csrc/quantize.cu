@@ -1018,6 +1018,7 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   bool valid_col = false;
   int64_t b = 0;
   bool any_nonfinite = false;
+  bool any_rare = false;  // a block marked kRareBlock: the rare-block pass has work
   int64_t it = 0;
   TileCursor cur(t_begin, P.n_row_tiles);
   for (int64_t t = t_begin; t < t_end; ++t, ++it, cur.advance(P.n_row_tiles)) {
@@ -1071,11 +1072,13 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
     }
     *reinterpret_cast<uint4*>(ostage + lane * 128 + ((warp ^ (lane & 7)) << 4)) = pk;
     sstage[lane * kTileBlocks + warp] = static_cast<uint8_t>(sc);
+    any_rare |= valid_col && rt * kTileRows + lane < P.rows && sc == kRareBlock;
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&out_full[buf]);
   }
   if (P.flags && __any_sync(0xffffffffu, any_nonfinite) && lane == 0) atomicOr(P.flags, MXW_FLAG_NONFINITE);
+  if (P.flags && __any_sync(0xffffffffu, any_rare) && lane == 0) atomicOr(P.flags, MXW_FLAG_RARE);
 }
 
 // ------------------------------------------------------ rare-block fixup
@@ -1136,6 +1139,8 @@ __device__ __forceinline__ void fixup_block(const QuantParams& P, int64_t idx) {
 
 template <int DT, int OBJ, int QM>
 __global__ void __launch_bounds__(256) quantize_fixup_kernel(const QuantParams P) {
+  // With a flag word, the main pass reported whether it marked any block.
+  if (P.flags && (*reinterpret_cast<volatile const uint32_t*>(P.flags) & MXW_FLAG_RARE) == 0) return;
   const int64_t total = P.rows * P.nb;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;

@@ -329,3 +329,22 @@ def test_close_call_blocks_match_oracle(objective, depth, pct, cuda_device) -> N
     p, s = _gpu(_to_device(w, cuda_device), cuda_device, **kw)
     po, so = oracle.quantize_mxfp4(w, **okw)
     assert_same_bytes(w, p, s, po, so)
+
+
+def test_rare_block_pass_runs_only_when_flagged(cuda_device) -> None:
+    """With a flag word, the main pass reports whether it marked any block for
+    the exact second pass (MXW_FLAG_RARE); the second pass skips its scan when
+    the bit is clear.  Bytes must match the oracle in both cases, and a bit
+    left set by an earlier call only makes later calls scan."""
+    rows, cols = 64, 1024
+    plain = syn.det_dense_weight(rows, cols, 31, outlier_fraction=0.01)
+    f = syn.bf16_bits_to_f32(plain).copy()
+    f[5, 64:96] = np.linspace(-3.0e38, 3.0e38, 32, dtype=np.float32)  # e >= 126 candidates: a rare block
+    rare = syn.f32_to_bf16_bits(f)
+    flags = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    for arr, expect_rare in ((plain, False), (rare, True), (plain, True)):
+        p, s = quantize_mxfp4(_to_device(arr, cuda_device), _flags=flags)
+        torch.cuda.synchronize(cuda_device)
+        assert bool(int(flags.item()) & _lib.MXW_FLAG_RARE) == expect_rare
+        po, so = oracle.quantize_mxfp4(arr)
+        assert_same_bytes(arr, p.cpu().numpy(), s.cpu().numpy(), po, so)
