@@ -47,7 +47,7 @@ METRIC = "bf16 weight GB/s quantized"
 # profiles/quantize_tma_kernel_gamma_d1_17408x5120.txt (178.33 MB + 26.55 MB).
 QUANT_TRAFFIC_BYTES = 178_330_112 + 26_546_432
 # The same for one X^T X launch (profiles/xtx_kernel_full_gram_65536x5120.txt).
-XTX_TRAFFIC_BYTES = 4_782_156_000 + 110_097_920
+XTX_TRAFFIC_BYTES = 1_693_721_000 + 90_838_528
 
 
 def _peaks() -> tuple[float, str]:
