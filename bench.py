@@ -44,8 +44,8 @@ WORKLOAD = (
 METRIC = "bf16 weight GB/s quantized"
 # dram__bytes_read.sum + dram__bytes_write.sum of one quantize launch of this
 # workload, from the ncu capture summarised in
-# profiles/quantize_tma_kernel_gamma_d1_17408x5120.txt (178.33 MB + 26.55 MB).
-QUANT_TRAFFIC_BYTES = 178_330_112 + 26_546_432
+# profiles/quantize_tma_kernel_gamma_d1_17408x5120.txt (178.37 MB + 26.45 MB).
+QUANT_TRAFFIC_BYTES = 178_365_184 + 26_449_920
 # The same for one X^T X launch (profiles/xtx_kernel_full_gram_65536x5120.txt).
 XTX_TRAFFIC_BYTES = 1_693_721_000 + 90_838_528
 
