@@ -213,6 +213,23 @@ MXW_API int mxw_accumulate_xtx(const void* x, int64_t tokens, int64_t cols, int6
                                int64_t ldg, uint32_t* flags, void* stream);
 
 /*
+ * The same product in the kernel's packed form, for token-sharded callers
+ * that all-reduce it: only the 128 x 256 tiles that reach the upper triangle,
+ * each stored row-major and added into its slot of `packed`
+ * (mxw_xtx_packed_floats(cols) floats, 16-byte aligned, zeroed by the caller
+ * before the first slice).  At cols = 5120 that is 420 tiles, 55 MB against
+ * the full Gram's 105 MB.  mxw_xtx_unpack then adds the packed tiles into a
+ * full Gram (the entries with column >= row and their transposes), giving
+ * the bits mxw_accumulate_xtx gives for the same slices.  Same requirements
+ * otherwise.  No counterpart in the reference, which forms only the diagonal
+ * blocks (mxwave/calibration.py:233-236).
+ */
+MXW_API size_t mxw_xtx_packed_floats(int64_t cols);
+MXW_API int mxw_accumulate_xtx_packed(const void* x, int64_t tokens, int64_t cols, int64_t ld, float* packed,
+                                      uint32_t* flags, void* stream);
+MXW_API int mxw_xtx_unpack(const float* packed, int64_t cols, float* gram, int64_t ldg, void* stream);
+
+/*
  * mean_abs = sum_abs / count, rms = sqrt(sum_sq / count) (either output may be
  * NULL).  Replaces ActivationCollector.finalize for the moment objectives
  * (mxwave/calibration.py:262-266).

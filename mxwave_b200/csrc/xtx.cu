@@ -54,6 +54,7 @@ struct XtxParams {
   int64_t tokens, cols, ldg, n_kblocks;
   int64_t n_col_tiles;  // 256-column tiles per row of tiles
   float* gram;
+  float* packed;  // non-null: add each tile's totals to its slot here instead of into gram
   uint32_t* flags;
 };
 
@@ -144,6 +145,58 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32
 
 // ------------------------------------------------------------------- kernel
 
+constexpr int kXtxTileFloats = kXtxBM * kXtxBN;
+
+// Tile `t` of the upper triangle, row by row: row tile `by` (128 rows) holds
+// the column tiles bx >= by / 2 (256 columns each), the first that reach
+// column >= row.  Returns (i0, j0), the tile's first row and column.
+__device__ __forceinline__ void xtx_tile_origin(int64_t t, int64_t n_col_tiles, int64_t& i0, int64_t& j0) {
+  int64_t by = 0;
+  for (;; ++by) {
+    const int64_t in_row = n_col_tiles - (by >> 1);
+    if (t < in_row) break;
+    t -= in_row;
+  }
+  i0 = by * kXtxBM;
+  j0 = ((by >> 1) + t) * kXtxBN;
+}
+
+// Adds one thread's 128 tile totals (row i0 + 32*quarter + lane, columns
+// j0 + 128*half ..) into G: the entries with column >= row in place, and the
+// transposes of those with column > row.  For one column the warp's 32 rows
+// are consecutive, so the transposed stores coalesce.
+__device__ __forceinline__ void add_tile_rows(float* gram, int64_t ldg, int64_t cols, int64_t i0, int64_t j0,
+                                              int quarter, int half, int lane, const float (&total)[128]) {
+  const int64_t r = i0 + 32 * quarter + lane;  // this thread's row of G
+  const int64_t cbase = j0 + 128 * half;        // its first column
+  if (cbase >= cols || cbase + 127 < i0 + 32 * quarter) return;
+  float* grow = gram + r * ldg + cbase;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int64_t c = cbase + 4 * k;
+    if (c >= r) {
+      float4 o = reinterpret_cast<float4*>(grow)[k];
+      o.x = __fadd_rn(o.x, total[4 * k]);
+      o.y = __fadd_rn(o.y, total[4 * k + 1]);
+      o.z = __fadd_rn(o.z, total[4 * k + 2]);
+      o.w = __fadd_rn(o.w, total[4 * k + 3]);
+      reinterpret_cast<float4*>(grow)[k] = o;
+    } else if (c + 3 >= r) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (c + u >= r) grow[4 * k + u] = __fadd_rn(grow[4 * k + u], total[4 * k + u]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 128; ++k) {
+    const int64_t c = cbase + k;
+    if (c > r) {
+      float* g = gram + c * ldg + r;
+      *g = __fadd_rn(*g, total[k]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kXtxThreads, 1)
     xtx_kernel(const __grid_constant__ CUtensorMap map, const XtxParams P) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -159,14 +212,8 @@ __global__ void __launch_bounds__(kXtxThreads, 1)
   // Tile blockIdx.x of the upper triangle, row by row: row tile `by` (128
   // rows) holds the column tiles bx >= by / 2 (256 columns each), the first
   // that reach column >= row.
-  int64_t by = 0, rem = blockIdx.x;
-  for (;; ++by) {
-    const int64_t in_row = P.n_col_tiles - (by >> 1);
-    if (rem < in_row) break;
-    rem -= in_row;
-  }
-  const int64_t i0 = by * kXtxBM;
-  const int64_t j0 = ((by >> 1) + rem) * kXtxBN;
+  int64_t i0, j0;
+  xtx_tile_origin(blockIdx.x, P.n_col_tiles, i0, j0);
   const int64_t n_chunks = (P.n_kblocks + kXtxChunkStages - 1) / kXtxChunkStages;
 
   if (threadIdx.x == 0) {
@@ -288,36 +335,22 @@ __global__ void __launch_bounds__(kXtxThreads, 1)
     if (!ok) atomicOr(fail, 1);
     // All epilogue warps agree before writing (named barrier 1, 256 threads).
     asm volatile("bar.sync 1, 256;" ::: "memory");
-    const int64_t r = i0 + 32 * quarter + lane;  // this thread's row of G
-    const int64_t cbase = j0 + 128 * half;        // its first column
-    if (*reinterpret_cast<volatile int*>(fail) == 0 && cbase < P.cols && cbase + 127 >= i0 + 32 * quarter) {
-      // Entries with column >= row, in place.
-      float* grow = P.gram + r * P.ldg + cbase;
+    if (*reinterpret_cast<volatile int*>(fail) == 0) {
+      if (P.packed) {
+        // This tile's totals, row-major 128 x 256, at its place in the packed buffer.
+        float4* pt = reinterpret_cast<float4*>(P.packed + static_cast<int64_t>(blockIdx.x) * kXtxTileFloats +
+                                               (32 * quarter + lane) * kXtxBN + 128 * half);
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const int64_t c = cbase + 4 * k;
-        if (c >= r) {
-          float4 o = reinterpret_cast<float4*>(grow)[k];
+        for (int k = 0; k < 32; ++k) {
+          float4 o = pt[k];
           o.x = __fadd_rn(o.x, total[4 * k]);
           o.y = __fadd_rn(o.y, total[4 * k + 1]);
           o.z = __fadd_rn(o.z, total[4 * k + 2]);
           o.w = __fadd_rn(o.w, total[4 * k + 3]);
-          reinterpret_cast<float4*>(grow)[k] = o;
-        } else if (c + 3 >= r) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (c + u >= r) grow[4 * k + u] = __fadd_rn(grow[4 * k + u], total[4 * k + u]);
+          pt[k] = o;
         }
-      }
-      // Their transposes below the diagonal: G[c, r] for c > r.  For one k
-      // the warp's 32 rows r are consecutive, so the stores coalesce.
-#pragma unroll
-      for (int k = 0; k < 128; ++k) {
-        const int64_t c = cbase + k;
-        if (c > r) {
-          float* g = P.gram + c * P.ldg + r;
-          *g = __fadd_rn(*g, total[k]);
-        }
+      } else {
+        add_tile_rows(P.gram, P.ldg, P.cols, i0, j0, quarter, half, lane, total);
       }
     }
   }
@@ -330,30 +363,56 @@ __global__ void __launch_bounds__(kXtxThreads, 1)
   if (threadIdx.x == 0 && *fail && P.flags) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
 }
 
+// Adds packed tile totals (the layout xtx_kernel writes with P.packed) into G.
+__global__ void __launch_bounds__(256) xtx_unpack_kernel(const float* __restrict__ packed, int64_t cols,
+                                                         int64_t n_col_tiles, float* gram, int64_t ldg) {
+  int64_t i0, j0;
+  xtx_tile_origin(blockIdx.x, n_col_tiles, i0, j0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const float4* src = reinterpret_cast<const float4*>(packed + static_cast<int64_t>(blockIdx.x) * kXtxTileFloats +
+                                                      (32 * quarter + lane) * kXtxBN + 128 * half);
+  float total[128];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const float4 v = src[k];
+    total[4 * k] = v.x;
+    total[4 * k + 1] = v.y;
+    total[4 * k + 2] = v.z;
+    total[4 * k + 3] = v.w;
+  }
+  add_tile_rows(gram, ldg, cols, i0, j0, quarter, half, lane, total);
+}
+
+static int64_t xtx_tiles(int64_t cols) {
+  const int64_t n_col_tiles = (cols + kXtxBN - 1) / kXtxBN;
+  int64_t n = 0;
+  for (int64_t by = 0; by < cols / kXtxBM; ++by) n += n_col_tiles - (by >> 1);
+  return n;
+}
+
 }  // namespace mxw
 
 using namespace mxw;
 
-extern "C" int mxw_accumulate_xtx(const void* x, int64_t tokens, int64_t cols, int64_t ld, float* gram,
-                                  int64_t ldg, uint32_t* flags, void* stream) {
-  if (tokens < 0 || cols <= 0 || cols % 128 != 0 || ld < cols || ld % 8 != 0 || ldg < cols || ldg % 4 != 0)
-    return MXW_EINVAL;
+static int accumulate_xtx(const void* x, int64_t tokens, int64_t cols, int64_t ld, float* gram, int64_t ldg,
+                          float* packed, uint32_t* flags, void* stream) {
+  if (tokens < 0 || cols <= 0 || cols % 128 != 0 || ld < cols || ld % 8 != 0) return MXW_EINVAL;
+  if (!packed && (ldg < cols || ldg % 4 != 0)) return MXW_EINVAL;
   if (tokens == 0) return MXW_OK;
-  if (!x || !gram) return MXW_EINVAL;
-  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(gram) % 16 != 0) return MXW_EINVAL;
+  if (!x || (!gram && !packed)) return MXW_EINVAL;
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(gram ? gram : packed) % 16 != 0)
+    return MXW_EINVAL;
   if (tokens >= (int64_t(1) << 31) || cols >= (int64_t(1) << 31)) return MXW_EINVAL;
   const size_t smem = 1024 + kXtxStages * kXtxStageBytes + (2 * kXtxStages + 4) * sizeof(uint64_t) + 16;
   const int rc = set_max_smem(reinterpret_cast<const void*>(xtx_kernel), smem);
   if (rc != MXW_OK) return rc;
   // One launch per slice of at most kXtxMaxTokens tokens: every on-device wait
   // stays far below the timeout, and each slice's TMEM accumulator is folded
-  // into the fp32 Gram before the next one starts.
-  // The tiles that reach the upper triangle: row tile by holds column tiles
-  // by/2 .. n_col_tiles-1.
+  // into the fp32 Gram before the next one starts.  Only the tiles that reach
+  // the upper triangle run.
   const int64_t n_col_tiles = (cols + kXtxBN - 1) / kXtxBN;
-  int64_t n_tiles = 0;
-  for (int64_t by = 0; by < cols / kXtxBM; ++by) n_tiles += n_col_tiles - (by >> 1);
-  const dim3 grid(static_cast<unsigned>(n_tiles));
+  const dim3 grid(static_cast<unsigned>(xtx_tiles(cols)));
   for (int64_t t0 = 0; t0 < tokens; t0 += kXtxMaxTokens) {
     const int64_t n = std::min<int64_t>(kXtxMaxTokens, tokens - t0);
     CUtensorMap map;
@@ -367,10 +426,37 @@ extern "C" int mxw_accumulate_xtx(const void* x, int64_t tokens, int64_t cols, i
     P.n_kblocks = (n + kXtxBK - 1) / kXtxBK;
     P.n_col_tiles = n_col_tiles;
     P.gram = gram;
+    P.packed = packed;
     P.flags = flags;
     xtx_kernel<<<grid, kXtxThreads, smem, static_cast<cudaStream_t>(stream)>>>(map, P);
     const int st = check_launch();
     if (st != MXW_OK) return st;
   }
   return MXW_OK;
+}
+
+extern "C" int mxw_accumulate_xtx(const void* x, int64_t tokens, int64_t cols, int64_t ld, float* gram,
+                                  int64_t ldg, uint32_t* flags, void* stream) {
+  if (!gram && tokens > 0) return MXW_EINVAL;
+  return accumulate_xtx(x, tokens, cols, ld, gram, ldg, nullptr, flags, stream);
+}
+
+extern "C" size_t mxw_xtx_packed_floats(int64_t cols) {
+  if (cols <= 0 || cols % 128 != 0 || cols >= (int64_t(1) << 31)) return 0;
+  return static_cast<size_t>(xtx_tiles(cols)) * kXtxTileFloats;
+}
+
+extern "C" int mxw_accumulate_xtx_packed(const void* x, int64_t tokens, int64_t cols, int64_t ld, float* packed,
+                                         uint32_t* flags, void* stream) {
+  if (!packed && tokens > 0) return MXW_EINVAL;
+  return accumulate_xtx(x, tokens, cols, ld, nullptr, 0, packed, flags, stream);
+}
+
+extern "C" int mxw_xtx_unpack(const float* packed, int64_t cols, float* gram, int64_t ldg, void* stream) {
+  if (cols <= 0 || cols % 128 != 0 || cols >= (int64_t(1) << 31) || ldg < cols || ldg % 4 != 0) return MXW_EINVAL;
+  if (!packed || !gram) return MXW_EINVAL;
+  if (reinterpret_cast<uintptr_t>(packed) % 16 != 0 || reinterpret_cast<uintptr_t>(gram) % 16 != 0) return MXW_EINVAL;
+  xtx_unpack_kernel<<<static_cast<unsigned>(xtx_tiles(cols)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      packed, cols, (cols + kXtxBN - 1) / kXtxBN, gram, ldg);
+  return check_launch();
 }

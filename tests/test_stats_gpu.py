@@ -148,6 +148,30 @@ def test_xtx_matches_fp64(tokens, cols, cuda_device) -> None:
     assert np.array_equal(got, got.T)
 
 
+@pytest.mark.parametrize("cols", [384, 640])
+def test_xtx_packed_then_unpacked_equals_direct(cols, cuda_device) -> None:
+    """Two token slices accumulated in the packed tile form and unpacked give
+    the direct path's Gram bit for bit (the all-reduce path of the bench)."""
+    lib = _lib.load()
+    x, _ = _x(3000, cols, cols + 5, cuda_device)
+    direct = torch.zeros(cols, cols, device=cuda_device)
+    n_packed = lib.mxw_xtx_packed_floats(cols)
+    n_tiles = sum((cols + 255) // 256 - (by >> 1) for by in range(cols // 128))
+    assert n_packed == n_tiles * 128 * 256
+    packed = torch.zeros(n_packed, device=cuda_device)
+    for a, b in ((0, 1234), (1234, 3000)):
+        part = x[a:b]
+        assert lib.mxw_accumulate_xtx(part.data_ptr(), b - a, cols, cols, direct.data_ptr(), cols, None,
+                                      _stream(cuda_device)) == 0
+        assert lib.mxw_accumulate_xtx_packed(part.data_ptr(), b - a, cols, cols, packed.data_ptr(), None,
+                                             _stream(cuda_device)) == 0
+    unpacked = torch.zeros(cols, cols, device=cuda_device)
+    assert lib.mxw_xtx_unpack(packed.data_ptr(), cols, unpacked.data_ptr(), cols, _stream(cuda_device)) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(direct, unpacked)
+    assert lib.mxw_xtx_packed_floats(100) == 0
+
+
 def test_xtx_accumulates_with_strides(cuda_device) -> None:
     lib = _lib.load()
     x, xf = _x(3000, 520, 12, cuda_device)
