@@ -318,7 +318,8 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
     """Calibration X^T X: 65536 x 5120 bf16 tokens -> full fp32 Gram on tcgen05.
 
     Tokens are split across ranks (strong scaling); each rank accumulates its
-    slice, then one NCCL all-reduce sums the 105 MB Gram.  Reported: whole-job
+    slice as packed upper-triangle tiles, one NCCL all-reduce sums those
+    (55 MB against the full Gram's 105 MB), and each rank unpacks the sum.  Reported: whole-job
     tokens/s (max over ranks), and the tensor roofline of the local kernel.
     """
     import torch
@@ -332,18 +333,29 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
     gram = torch.zeros(k, k, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    # Several GPUs: each rank accumulates the packed upper-triangle tiles (55 MB
+    # at 5120 channels instead of the full 105 MB Gram), NCCL sums those, and
+    # every rank unpacks the sum into its full Gram.
+    packed = torch.zeros(lib.mxw_xtx_packed_floats(k), device=dev) if world > 1 else None
+
     def step(record=None) -> None:
-        gram.zero_()
+        (packed if world > 1 else gram).zero_()
         if record is not None:
             record[0].record(stream)
-        _lib.check(lib.mxw_accumulate_xtx(x.data_ptr(), hi - lo, k, k, gram.data_ptr(), k, None,
-                                          stream.cuda_stream), "xtx")
+        if world > 1:
+            _lib.check(lib.mxw_accumulate_xtx_packed(x.data_ptr(), hi - lo, k, k, packed.data_ptr(), None,
+                                                     stream.cuda_stream), "xtx")
+        else:
+            _lib.check(lib.mxw_accumulate_xtx(x.data_ptr(), hi - lo, k, k, gram.data_ptr(), k, None,
+                                              stream.cuda_stream), "xtx")
         if record is not None:
             record[1].record(stream)
         if world > 1:
             import torch.distributed as dist
 
-            dist.all_reduce(gram, op=dist.ReduceOp.SUM)
+            dist.all_reduce(packed, op=dist.ReduceOp.SUM)
+            gram.zero_()
+            _lib.check(lib.mxw_xtx_unpack(packed.data_ptr(), k, gram.data_ptr(), k, stream.cuda_stream), "unpack")
 
     for _ in range(args.warmup):
         step()
@@ -382,7 +394,9 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
         "unit": "tokens/s",
         "scaling": "strong",
         "config": {"workload": f"full (symmetric) X^T X of {total_tokens} x {k} bf16 activations -> fp32 Gram, "
-                               f"tokens split over {world} GPU(s), NCCL all-reduce of the Gram"},
+                               f"tokens split over {world} GPU(s)"
+                               + (", NCCL all-reduce of the packed upper-triangle tiles, unpacked into the Gram"
+                                  if world > 1 else "")},
         "ms_per_step": round(ms / args.steps, 4),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak[0], "unit": "TFLOP/s",
                      "frac": round(achieved / peak[0], 4), "peak_kind": peak[1], "kernel": "xtx_kernel (tcgen05)",
