@@ -284,15 +284,18 @@ __global__ void stats_plain_kernel(const void* __restrict__ x, int64_t ld, StatP
   }
 }
 
-// Token slices per strip (the cluster size): up to 4, keeping at least 8
-// tiles per slice.  Measured on B200 at 5120 channels: 8192 tokens take
-// 31 us with 4 slices against 39 us with 1 or 8 (one slice leaves too few
-// loads in flight per SM; 8 short slices pay the per-CTA set-up and the two
-// cluster barriers more often than they gain).
+// Token slices per strip (the cluster size).  Measured on B200 at 5120
+// channels, bf16 moments, L2 flushed before each launch (slices: time):
+//   4096 tokens (16 tiles):  2: 22.5 us
+//   8192 tokens (32 tiles):  2: 32.8 us, 4: 38.9 us
+//   16384 tokens (64 tiles): 2: 53.2 us, 4: 57.3 us
+//   65536 tokens (256 tiles): 2: 176 us, 4: 152 us
+// Four slices pay off only once each slice still has 32 tiles; below that the
+// second partial wave of CTAs and the per-CTA set-up and cluster barriers
+// cost more than the extra loads in flight gain.  One slice below 16 tiles.
 static int stat_slices(int64_t tiles) {
-  int S = 1;
-  while (S < 4 && tiles >= 8 * (2 * S)) S *= 2;
-  return S;
+  if (tiles < 16) return 1;
+  return tiles < 128 ? 2 : 4;
 }
 
 template <int DT, bool M, bool G>
