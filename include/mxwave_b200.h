@@ -135,8 +135,9 @@ MXW_API int mxw_error_sums(const void* original, int dtype, int64_t rows, int64_
  * exits.  A launch that would need more scratch returns MXW_EUNSUPPORTED (use
  * mxw_error_sums with a workspace instead).  The call allocates nothing: it
  * clears the ticket with an asynchronous memset on `stream`, then launches.
- * The first call on a device looks up the array's device address (and may
- * load this library's kernels onto that device): make that first call before
+ * Every call looks up the array's device address in the current context
+ * (so it stays valid across cudaDeviceReset); the first call in a context may
+ * load this library's kernels onto the device: make that first call before
  * any stream capture.  All calls share the one array, so calls that overlap
  * on the device (other streams, other host threads) race and must not be
  * issued concurrently.

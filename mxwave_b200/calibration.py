@@ -62,10 +62,6 @@ def validate_statistic(target_name: str, objective: str, tensor: torch.Tensor, w
         raise ValueError(f"Calibration Hessian is not symmetric: {target_name}")
 
 
-def _stream(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
-
-
 def accumulate_stats(
     x: torch.Tensor,
     sum_abs: torch.Tensor | None,
@@ -79,19 +75,11 @@ def accumulate_stats(
         x = x.to(torch.float32)
     if x.stride(-1) != 1 or (x.shape[0] > 1 and x.stride(0) < x.shape[1]):
         x = x.contiguous()
-    tokens, width = x.shape
-    if tokens == 0:
+    if x.shape[0] == 0:
         return
-    lib = _lib.load()
-    with torch.cuda.device(x.device):
-        status = lib.mxw_accumulate_activation_stats(
-            x.data_ptr(), _DTYPE_CODES[x.dtype], tokens, width, max(x.stride(0), width),
-            None if sum_abs is None else sum_abs.data_ptr(),
-            None if sum_sq is None else sum_sq.data_ptr(),
-            None if gram_blocks is None else gram_blocks.data_ptr(),
-            None, _stream(x.device),
-        )
-    _lib.check(status, "mxw_accumulate_activation_stats")
+    from . import ops  # noqa: F401  -- registers torch.ops.mxwave_b200
+
+    torch.ops.mxwave_b200.accumulate_activation_stats_(x, sum_abs, sum_sq, gram_blocks)
 
 
 class ActivationCollector:
@@ -217,7 +205,8 @@ class ActivationCollector:
         if missing:
             raise ValueError(f"Calibration hooks did not observe {len(missing)} target(s): {missing[:5]}")
         result: dict[str, dict[str, torch.Tensor]] = {}
-        lib = _lib.load()
+        from . import ops  # noqa: F401  -- registers torch.ops.mxwave_b200
+
         for objective in sorted(self.objectives):
             values: dict[str, torch.Tensor] = {}
             for name in sorted(self.target_widths):
@@ -225,26 +214,18 @@ class ActivationCollector:
                 width = self.target_widths[name]
                 if objective == "mean-abs":
                     src = self._absolute_sums[name]
-                    value = torch.empty_like(src)
                     with torch.cuda.device(src.device):
-                        _lib.check(lib.mxw_finalize_moments(src.data_ptr(), None, width, count, value.data_ptr(),
-                                                            None, _stream(src.device)), "mxw_finalize_moments")
+                        value = torch.ops.mxwave_b200.finalize_moments(src, count, False)
                 elif objective == "rms":
                     src = self._square_sums[name]
-                    value = torch.empty_like(src)
                     with torch.cuda.device(src.device):
-                        _lib.check(lib.mxw_finalize_moments(None, src.data_ptr(), width, count, None,
-                                                            value.data_ptr(), _stream(src.device)),
-                                   "mxw_finalize_moments")
+                        value = torch.ops.mxwave_b200.finalize_moments(src, count, True)
                 else:
                     src = self._gram_sums[name]
-                    value = torch.empty_like(src)
                     mode = _lib.MXW_DAMP_ABSOLUTE if self.hessian_damp_mode == "absolute" else _lib.MXW_DAMP_RELATIVE
                     with torch.cuda.device(src.device):
-                        _lib.check(lib.mxw_finalize_block_hessian(src.data_ptr(), 0, width, width, count,
-                                                                  float(self.hessian_damp), mode, value.data_ptr(),
-                                                                  _stream(src.device)),
-                                   "mxw_finalize_block_hessian")
+                        value = torch.ops.mxwave_b200.finalize_block_hessian(src, False, count,
+                                                                             float(self.hessian_damp), mode)
                 if to_cpu:
                     value = value.cpu().to(torch.float32).contiguous()
                 validate_statistic(name, objective, value, width)

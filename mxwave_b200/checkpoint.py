@@ -2,9 +2,10 @@
 
 * ``tensor_chunk_rows`` and ``iter_quantized_row_chunks`` keep the reference
   contract (mxwave/checkpoint.py:89-126): the same row-chunk bound, the same
-  shape and finiteness errors (same messages), chunks yielded in order.  The
-  loop reads the next chunks on a background thread while the current one is
-  quantized, and when ``quantize`` is this package's quantizer the NaN/inf
+  shape and finiteness errors (same messages), chunks yielded in order.  With
+  this package's own row reader the loop reads the next chunks on a
+  background thread while the current one is quantized (other readers are
+  called on the caller's thread), and when ``quantize`` is this package's quantizer the NaN/inf
   check is folded into the kernel (a device flag word) instead of a separate
   ``isfinite`` reduction; the flag is read before the chunk is yielded, so a
   bad chunk still raises before anything of it is returned.
@@ -74,9 +75,21 @@ def iter_quantized_row_chunks(
     max_rows: int,
     max_elements: int,
     name: str,
-    prefetch: int = 2,
+    prefetch: int | None = None,
 ) -> Iterator[tuple[int, int, torch.Tensor, torch.Tensor]]:
-    """Read, validate, and quantize one element-bounded row slice at a time."""
+    """Read, validate, and quantize one element-bounded row slice at a time.
+
+    ``prefetch`` chunks are read ahead on a background thread while the
+    current one is quantized.  Peak memory is then (prefetch + 1) chunks
+    instead of the reference's one, and ``read_rows`` is called from that
+    thread, concurrently with the caller.  The default (None) prefetches 2
+    chunks only when ``read_rows`` is this package's ``read_tensor_row_range``
+    (which opens the file per call and is thread-safe) and reads on the
+    caller's thread otherwise, as the reference does.
+    """
+    if prefetch is None:
+        reader = read_rows.func if isinstance(read_rows, functools.partial) else read_rows
+        prefetch = 2 if reader is read_tensor_row_range else 0
     chunk_rows = tensor_chunk_rows(columns, max_rows, max_elements)
     bounds = [(start, min(start + chunk_rows, rows)) for start in range(0, rows, chunk_rows)]
     if not bounds:

@@ -141,48 +141,51 @@ def quantize_mxfp4(
             _gamma_ok.add(gamma)
         gamma_f32 = gamma.to(device=device, dtype=torch.float32).contiguous()
 
-    w, dtype_code = _as_kernel_input(tensor)
-    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=device)
-    scales = torch.empty((rows, num_blocks), dtype=torch.uint8, device=device)
+    w, _dtype_code = _as_kernel_input(tensor)
     if rows == 0:
-        return packed, scales
-    lib = _lib.load()
-    with torch.cuda.device(device):
-        status = lib.mxw_quantize_mxfp4(
-            w.data_ptr(),
-            dtype_code,
-            rows,
-            cols,
-            w.stride(0),
-            float(scale_percentile),
-            None if gamma_f32 is None else gamma_f32.data_ptr(),
-            None if hessian_f32 is None else hessian_f32.data_ptr(),
-            _lib.MXW_METHOD_RTN if method == "rtn" else _lib.MXW_METHOD_MSE,
-            mse_clip_depth,
-            packed.data_ptr(),
-            scales.data_ptr(),
-            (_flags if _flags is not None else _device_flags(device)).data_ptr(),
-            _stream_handle(device),
-        )
-    _lib.check(status, "mxw_quantize_mxfp4")
-    return packed, scales
+        return (torch.empty((0, cols // 2), dtype=torch.uint8, device=device),
+                torch.empty((0, num_blocks), dtype=torch.uint8, device=device))
+    _ops()
+    return torch.ops.mxwave_b200.quantize_mxfp4(
+        w,
+        float(scale_percentile),
+        gamma_f32,
+        hessian_f32,
+        _lib.MXW_METHOD_RTN if method == "rtn" else _lib.MXW_METHOD_MSE,
+        mse_clip_depth,
+        _flags if _flags is not None else _device_flags(device),
+    )
+
+
+def _ops():
+    """Register the torch operators (mxwave_b200.ops) on first use."""
+    from . import ops
+
+    return ops
 
 
 _DEVICE_FLAGS: dict = {}
 
 
 def _device_flags(device: torch.device) -> torch.Tensor:
-    """A per-device flag word for calls that pass none.
+    """A flag word for calls that pass none: one per (device, stream), cleared before each use.
 
-    Its MXW_FLAG_RARE bit lets the kernel skip the rare-block scan after a
-    main pass that marked nothing; the bits are sticky, so sharing the word
-    between calls and streams only costs extra scans.
+    Its MXW_FLAG_RARE bit lets the rare-block pass return at once after a
+    main pass that marked nothing, so it is zeroed on the current stream
+    before every call; a bit left over from an earlier call would make every
+    later call scan the scale bytes again.  Calls on one stream run in order,
+    so the clear cannot race with an earlier call's rare-block pass; each
+    stream has its own word for the same reason.  Nothing reads its
+    MXW_FLAG_NONFINITE bit; callers that need it pass their own word.
     """
-    key = (device.type, device.index)
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
     flags = _DEVICE_FLAGS.get(key)
     if flags is None:
         flags = torch.zeros(1, dtype=torch.int32, device=device)
         _DEVICE_FLAGS[key] = flags
+    else:
+        flags.zero_()
     return flags
 
 
@@ -232,16 +235,8 @@ def dequant_mxfp4(
     _require_cuda(packed, "packed")
     cols = shape[-1]
     rows = math.prod(shape) // cols
-    p = packed.reshape(rows, cols // 2).contiguous()
-    s = scales.reshape(rows, cols // BLOCK_SIZE).to(device=packed.device).contiguous()
-    out = torch.empty((rows, cols), dtype=torch.float32, device=packed.device)
-    lib = _lib.load()
-    with torch.cuda.device(packed.device):
-        status = lib.mxw_dequant_mxfp4(
-            p.data_ptr(), s.data_ptr(), rows, cols, out.data_ptr(), _stream_handle(packed.device)
-        )
-    _lib.check(status, "mxw_dequant_mxfp4")
-    return out.reshape(shape)
+    _ops()
+    return torch.ops.mxwave_b200.dequant_mxfp4(packed, scales, rows, cols).reshape(shape)
 
 
 def _damp_block_hessian(hessian: torch.Tensor, damp: float, mode: HessianDampingMode) -> None:
@@ -273,25 +268,16 @@ def compute_block_hessian(
     if damp_mode not in ("absolute", "relative"):
         raise ValueError(f"Unknown Hessian damping mode: {damp_mode}")
     _require_cuda(X, "X")
-    x, dtype_code = _as_kernel_input(X)
+    x, _dtype_code = _as_kernel_input(X)
     device = X.device
     gram = torch.zeros((K // BLOCK_SIZE, BLOCK_SIZE, BLOCK_SIZE), dtype=torch.float32, device=device)
-    out = torch.empty_like(gram)
-    lib = _lib.load()
-    stream = _stream_handle(device)
-    with torch.cuda.device(device):
-        if N > 0:
-            _lib.check(
-                lib.mxw_accumulate_block_gram(x.data_ptr(), dtype_code, N, K, x.stride(0), gram.data_ptr(), stream),
-                "mxw_accumulate_block_gram",
-            )
-        status = lib.mxw_finalize_block_hessian(
-            gram.data_ptr(), 0, K, K, max(N, 1), float(damp),
-            _lib.MXW_DAMP_ABSOLUTE if damp_mode == "absolute" else _lib.MXW_DAMP_RELATIVE,
-            out.data_ptr(), stream,
-        )
-    _lib.check(status, "mxw_finalize_block_hessian")
-    return out
+    _ops()
+    if N > 0:
+        torch.ops.mxwave_b200.accumulate_activation_stats_(x, None, None, gram)
+    return torch.ops.mxwave_b200.finalize_block_hessian(
+        gram, False, max(N, 1), float(damp),
+        _lib.MXW_DAMP_ABSOLUTE if damp_mode == "absolute" else _lib.MXW_DAMP_RELATIVE,
+    )
 
 
 __all__ = [

@@ -864,12 +864,13 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
   best = nan_min(best, e_f1);
   bool run_safe = need_safe;
   if (!GAMMA && __any_sync(0xffffffffu, run_safe)) {
-    // The safe candidate (f+2) comes last, so it wins only with an error
-    // strictly below `best`.  Every E2M1 value at scale f+2 is a multiple of
-    // 2^(f+1), so each element's error is at least its distance to that
-    // lattice: (2^(f+1) * |v - rint(v)|)^2 with v = t / 2^(f+1) (rint by the
-    // 1.5 * 2^23 add, exact for |v| <= 12 here).  Measured: a 2 % gain
-    // unweighted; with gamma weights the extra loads cost more than it saves.
+    // Unweighted objective only.  The safe candidate (f+2) comes last, so it
+    // wins only with an error strictly below `best`.  Every E2M1 value at
+    // scale f+2 is a multiple of 2^(f+1), so each element's error is at least
+    // its distance to that lattice: (2^(f+1) * |v - rint(v)|)^2 with
+    // v = t / 2^(f+1) (rint by the 1.5 * 2^23 add, exact for |v| <= 12 here).
+    // Measured: a 2 % gain unweighted; with gamma weights the extra loads cost
+    // more than it saves, so weighted blocks skip the bound.
     const float iv = exp2i(-(f + 1));
     const unsigned long long IV = pack2(iv, iv), M2 = pack2(12582912.0f, 12582912.0f);
     const unsigned long long NM2 = pack2(-12582912.0f, -12582912.0f), NEG2 = pack2(-1.0f, -1.0f);
@@ -878,11 +879,7 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
     for (int j = 0; j < 16; ++j) {
       const unsigned long long v = mul2(t2[j], IV);
       const unsigned long long r = fma2(add2(add2(v, M2), NM2), NEG2, v);  // v - rint(v)
-      if constexpr (GAMMA) {
-        acc = fma2(mul2(r, r), load_g2(Gw, j), acc);
-      } else {
-        acc = fma2(r, r, acc);
-      }
+      acc = fma2(r, r, acc);
     }
     const f2 a2 = unpack2(acc);
     const float lb = __fmul_rn(__fmul_rn(__fadd_rn(a2.x, a2.y), exp2i(2 * f + 2)), 0.03125f);

@@ -20,7 +20,6 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
-#include <mutex>
 
 #include "common.cuh"
 #include "runtime.h"
@@ -256,35 +255,22 @@ constexpr size_t kNoAllocScratchBytes = 16 + static_cast<size_t>(kNoAllocMaxCtas
 
 static __device__ __align__(256) unsigned char g_error_sums_scratch[kNoAllocScratchBytes];
 
-// Device address of g_error_sums_scratch on the current device.  In host code
-// the array's name is only a host-side stand-in, so the address comes from
-// cudaGetSymbolAddress, once per device (the first call on a device may also
-// load this module onto it).
+// Device address of g_error_sums_scratch in the current device's context.
+// In host code the array's name is only a host-side stand-in, so the address
+// comes from cudaGetSymbolAddress.  It is looked up on every call rather than
+// cached: a cached address would go stale after cudaDeviceReset or a new
+// primary context, and once this module is loaded the lookup is a table
+// search.  The first call in a context may also load this module onto the
+// device.
 static void* noalloc_scratch(int* status) {
-  static std::mutex mu;
-  static void* addr[64] = {nullptr};
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&p, g_error_sums_scratch);
   if (err != cudaSuccess) {
     *status = record_cuda_error(err);
     return nullptr;
   }
-  if (dev < 0 || dev >= 64) {
-    *status = MXW_EUNSUPPORTED;
-    return nullptr;
-  }
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    err = cudaGetSymbolAddress(&p, g_error_sums_scratch);
-    if (err != cudaSuccess) {
-      *status = record_cuda_error(err);
-      return nullptr;
-    }
-    addr[dev] = p;
-  }
   *status = MXW_OK;
-  return addr[dev];
+  return p;
 }
 
 }  // namespace mxw

@@ -30,6 +30,8 @@ mxwave.gguf.repack_mxfp4_blocks        mxwave_b200.gguf.repack_mxfp4_blocks
 mxwave.calibration.save_calibration_data / open_calibration_data
   calibration_cli.py:474  engine.py:500
                                        mxwave_b200.calibration_artifact (device hand-off)
+mxwave.engine._quantized_chunks        mxwave_b200.engine_stream.quantized_chunks
+  engine.py:428,630                    (file -> pinned -> HBM -> pinned pipeline per tensor)
 =====================================  ============================================
 
 The engines keep their planning, durability, manifests and CLI; only the
@@ -56,10 +58,14 @@ class Installation:
         for module, name, value in reversed(self.saved):
             setattr(module, name, value)
         self.saved.clear()
+        from . import engine_stream
+
+        engine_stream.set_original(None)
 
 
 def _replacements() -> dict[str, dict[str, Any]]:
-    from . import calibration, calibration_artifact, calibration_stream, checkpoint, core, gguf, routed_calibration, verify
+    from . import (calibration, calibration_artifact, calibration_stream, checkpoint, core, engine_stream, gguf,
+                   routed_calibration, verify)
 
     return {
         "mxwave.core": {
@@ -76,6 +82,7 @@ def _replacements() -> dict[str, dict[str, Any]]:
             "channel_weighted_sqnr": verify.channel_weighted_sqnr,
             "block_hessian_weighted_sqnr": verify.block_hessian_weighted_sqnr,
             "open_calibration_data": calibration_artifact.open_calibration_data,
+            "_quantized_chunks": engine_stream.quantized_chunks,
         },
         "mxwave.expert_engine": {
             "quantize_mxfp4": core.quantize_mxfp4,
@@ -131,6 +138,12 @@ def install() -> Installation:
         from . import calibration_artifact
 
         calibration_artifact._capture_originals()  # it calls the reference's own writer/reader
+    if "mxwave.engine" in modules:
+        from . import engine_stream
+
+        # Tensors the stream does not take (another quantizer patched in, a CPU
+        # device) go through the engine's own chunk loop.
+        engine_stream.set_original(getattr(modules["mxwave.engine"], "_quantized_chunks", None))
     for module_name, names in _replacements().items():
         module = modules.get(module_name)
         if module is None:

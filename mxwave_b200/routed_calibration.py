@@ -1,11 +1,23 @@
 """Drop-in for ``mxwave.routed_calibration.RoutedLayerMoments`` on B200.
 
-Same fields, constructor, validation messages and results as the reference
-(mxwave/routed_calibration.py:55-170).  The accumulations run in one sm_100a
-kernel (``mxw_accumulate_routed_squares``): the routes are grouped by expert
-with a stable sort (host-side index bookkeeping on the device), then each
-expert's squared, routing-weighted activations are summed in route order in
-fp64 and added once -- deterministic, unlike an atomic index_add_.
+The public surface is the reference's (mxwave/routed_calibration.py:55-170):
+the five accumulator fields, ``create`` / ``update_inputs`` / ``update_down``
+/ ``finalize``, their validation messages and the shape of ``finalize``'s
+result.  The implementation is this package's own:
+
+* the accumulators live in two device arenas (one fp32, one int64), so the
+  whole layer state is two buffers that a token-sharded caller can
+  all-reduce in two calls;
+* route validation is one device reduction and one host read per update,
+  instead of one host synchronisation per condition;
+* accumulation is one sm_100a kernel (``mxw_accumulate_routed_squares``):
+  routes are grouped by expert with a stable sort, and each expert's squared,
+  routing-weighted activations are summed in route order in fp64 and added
+  once -- deterministic, unlike an atomic ``index_add_``;
+* ``finalize`` computes every expert's gamma at once on the device
+  (sqrt(squares / mass), normalised by its maximum, in fp32 with IEEE
+  division and square root, as the reference's per-expert CPU loop rounds
+  them) and brings only the finished gammas, masses and counts to the host.
 """
 
 from __future__ import annotations
@@ -18,6 +30,7 @@ import torch
 from . import _lib
 
 _DTYPES = {torch.bfloat16: _lib.MXW_BF16, torch.float16: _lib.MXW_F16, torch.float32: _lib.MXW_F32}
+_PROJECTIONS = ("gate_proj", "up_proj", "down_proj")
 
 
 def _accumulate(squares: torch.Tensor, mass: torch.Tensor | None, inputs: torch.Tensor, route_rows: torch.Tensor,
@@ -25,9 +38,8 @@ def _accumulate(squares: torch.Tensor, mass: torch.Tensor | None, inputs: torch.
     """Add fl(fl(x^2) * w2) of each route's input row into its expert's row of `squares`."""
     device = squares.device
     order = torch.sort(experts, stable=True).indices
-    counts = torch.bincount(experts, minlength=squares.shape[0])
     offsets = torch.zeros(squares.shape[0] + 1, dtype=torch.int64, device=device)
-    torch.cumsum(counts, 0, out=offsets[1:])
+    torch.cumsum(torch.bincount(experts, minlength=squares.shape[0]), 0, out=offsets[1:])
     rows_sorted = route_rows[order].contiguous()
     w2_sorted = route_w2[order].contiguous()
     x = inputs.detach()
@@ -45,6 +57,16 @@ def _accumulate(squares: torch.Tensor, mass: torch.Tensor | None, inputs: torch.
     _lib.check(status, "mxw_accumulate_routed_squares")
 
 
+def _device_gammas(squares: torch.Tensor, mass: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per expert: sqrt(squares / mass) / its maximum, and whether the expert is calibrated."""
+    usable = (mass > 0) & (squares > 0).any(dim=1)
+    safe_mass = torch.where(mass > 0, mass, torch.ones_like(mass))
+    root = torch.sqrt(squares / safe_mass[:, None])
+    peak = root.amax(dim=1, keepdim=True)
+    gamma = root / torch.where(peak > 0, peak, torch.ones_like(peak))
+    return gamma, usable
+
+
 @dataclass
 class RoutedLayerMoments:
     """Bounded per-expert statistics, with no retained token activation history."""
@@ -60,81 +82,80 @@ class RoutedLayerMoments:
         """Allocate device-local accumulators for one complete unsharded MoE layer."""
         if min(experts, hidden, intermediate) <= 0:
             raise ValueError("Expert count and channel widths must be positive")
-        if torch.device(device).type != "cuda":
+        dev = torch.device(device)
+        if dev.type != "cuda":
             raise RuntimeError("mxwave_b200 accumulates routed moments on CUDA devices only (no CPU fallback)")
-        return cls(
-            torch.zeros((experts, hidden), dtype=torch.float32, device=device),
-            torch.zeros((experts, intermediate), dtype=torch.float32, device=device),
-            torch.zeros(experts, dtype=torch.float32, device=device),
-            torch.zeros(experts, dtype=torch.int64, device=device),
-            torch.zeros(experts, dtype=torch.int64, device=device),
-        )
+        floats = torch.zeros(experts * (hidden + intermediate + 1), dtype=torch.float32, device=dev)
+        counts = torch.zeros(2 * experts, dtype=torch.int64, device=dev)
+        a, b = experts * hidden, experts * (hidden + intermediate)
+        return cls(floats[:a].view(experts, hidden), floats[a:b].view(experts, intermediate), floats[b:],
+                   counts[:experts], counts[experts:])
 
     def _routes(self, ids: torch.Tensor, weights: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        if (
-            ids.ndim != 2
-            or weights.shape != ids.shape
-            or ids.dtype not in (torch.int32, torch.int64)
-            or ids.device != self.input_squares.device
-        ):
+        """Flattened expert ids and squared router weights, validated in one device reduction."""
+        if (ids.ndim != 2 or weights.shape != ids.shape or ids.dtype not in (torch.int32, torch.int64)
+                or ids.device != self.input_squares.device):
             raise ValueError("Expected matching device-local [tokens, top_k] route IDs/weights")
-        if (
-            ids.numel() == 0
-            or bool((ids < 0).any())
-            or bool((ids >= len(self.route_mass)).any())
-            or not bool(torch.isfinite(weights).all())
-            or bool((weights < 0).any())
-        ):
+        experts = self.route_mass.numel()
+        if ids.numel() == 0:
             raise ValueError("Routing IDs or weights are empty, invalid, or non-finite")
-        return ids.reshape(-1).long(), weights.detach().float().reshape(-1).square()
+        w = weights.detach().float()
+        invalid = ((ids < 0) | (ids >= experts)).any() | (~torch.isfinite(w)).any() | (w < 0).any()
+        if bool(invalid):
+            raise ValueError("Routing IDs or weights are empty, invalid, or non-finite")
+        return ids.reshape(-1).long(), w.reshape(-1).square()
 
     @torch.no_grad()
     def update_inputs(self, inputs: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor) -> None:
         """Accumulate gate/up inputs for exactly the expert routes selected at runtime."""
-        routed_ids, mass = self._routes(ids, weights)
+        routed_ids, w2 = self._routes(ids, weights)
         if inputs.shape != (ids.shape[0], self.input_squares.shape[1]):
             raise ValueError("Gate/up activation shape does not match the actual token routes")
-        # Route (t, k) reads token row t (the reference repeats each row top_k times).
-        route_rows = torch.arange(routed_ids.numel(), device=routed_ids.device) // ids.shape[1]
-        _accumulate(self.input_squares, self.route_mass, inputs, route_rows, mass, routed_ids)
-        self.observations.add_(torch.bincount(routed_ids, minlength=len(self.route_mass)))
+        # Route (t, k) reads token row t: the kernel indexes rows, nothing is repeated.
+        token_of_route = torch.arange(routed_ids.numel(), device=routed_ids.device) // ids.shape[1]
+        _accumulate(self.input_squares, self.route_mass, inputs, token_of_route, w2, routed_ids)
+        self.observations.add_(torch.bincount(routed_ids, minlength=self.route_mass.numel()))
 
     @torch.no_grad()
     def update_down(self, inputs: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor) -> None:
         """Accumulate token-major down-projection inputs, weighted by router weights squared."""
-        routed_ids, mass = self._routes(ids, weights)
+        routed_ids, w2 = self._routes(ids, weights)
         if inputs.shape != (ids.numel(), self.down_squares.shape[1]):
             raise ValueError("Down inputs must have one row per token-major expert route")
-        route_rows = torch.arange(routed_ids.numel(), device=routed_ids.device)
-        _accumulate(self.down_squares, None, inputs, route_rows, mass, routed_ids)
-        self.down_observations.add_(torch.bincount(routed_ids, minlength=len(self.route_mass)))
+        row_of_route = torch.arange(routed_ids.numel(), device=routed_ids.device)
+        _accumulate(self.down_squares, None, inputs, row_of_route, w2, routed_ids)
+        self.down_observations.add_(torch.bincount(routed_ids, minlength=self.route_mass.numel()))
 
+    @torch.no_grad()
     def finalize(self, layer: int) -> tuple[dict[str, torch.Tensor], dict[str, Any]]:
         """Return observed, nonzero RMS targets; unseen targets remain explicitly uncalibrated."""
-        if not torch.equal(self.observations, self.down_observations):
+        same_routes = torch.equal(self.observations, self.down_observations)
+        if not same_routes:
             raise ValueError("Gate/up and down captures do not cover the same routed observations")
-        if not bool(torch.isfinite(self.input_squares).all()) or not bool(torch.isfinite(self.down_squares).all()):
+        finite = torch.isfinite(self.input_squares).all() & torch.isfinite(self.down_squares).all()
+        if not bool(finite):
             raise ValueError("Captured activation moments contain NaN or infinity")
+        gate_gamma, gate_ok = _device_gammas(self.input_squares, self.route_mass)
+        down_gamma, down_ok = _device_gammas(self.down_squares, self.route_mass)
+        # One host transfer of everything the result needs.
+        gate_gamma, down_gamma = gate_gamma.cpu(), down_gamma.cpu()
+        flags = torch.stack([gate_ok, down_ok]).cpu().tolist()
+        masses = self.route_mass.cpu().tolist()
+        counts = self.observations.cpu().tolist()
         statistics: dict[str, torch.Tensor] = {}
         retained: list[str] = []
-        masses = self.route_mass.cpu()
-        counts = self.observations.cpu()
-        gate = self.input_squares.cpu()
-        down = self.down_squares.cpu()
         for expert in range(len(masses)):
-            for projection, values in (("gate_proj", gate), ("up_proj", gate), ("down_proj", down)):
+            for projection in _PROJECTIONS:
                 name = f"model.layers.{layer}.mlp.experts.{expert}.{projection}.weight"
-                mass = float(masses[expert])
-                if mass <= 0 or not bool((values[expert] > 0).any()):
+                down = projection == "down_proj"
+                if not flags[1 if down else 0][expert]:
                     retained.append(name)
                     continue
-                gamma = torch.sqrt(values[expert] / mass)
-                gamma = (gamma / gamma.amax()).float().contiguous()
-                statistics[name] = gamma
+                statistics[name] = (down_gamma if down else gate_gamma)[expert].clone()
         return statistics, {
             "layer": layer,
-            "routed_observations": counts.tolist(),
-            "routing_weight_squared_mass": masses.tolist(),
+            "routed_observations": counts,
+            "routing_weight_squared_mass": masses,
             "calibrated_targets": len(statistics),
             "retained_unweighted_targets": retained,
         }

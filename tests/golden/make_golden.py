@@ -3,6 +3,7 @@
 Run in a container where the reference MxWave checkout is importable:
 
     python tests/golden/make_golden.py --reference /path/to/MxWave
+    python tests/golden/make_golden.py --reference /path/to/MxWave --only-layers
 
 It imports the reference's own ``mxwave.core.quantize_mxfp4`` and
 ``mxwave.calibration.ActivationCollector`` (CPU, fp32) and records:
@@ -19,6 +20,11 @@ It imports the reference's own ``mxwave.core.quantize_mxfp4`` and
 
 Weights are quantized through the reference's ``iter_quantized_row_chunks``
 with its default 1,048,576-element chunks, as its engine does.
+
+``--only-layers`` runs ``layer_golden.py``: the decoder-layer workload (the
+reference's sequential calibration of a random-init layer, then all seven
+linears) and the whole-checkpoint workload (one more layer plus a 128-expert
+stack, block-Hessian weighted).
 """
 
 from __future__ import annotations
@@ -33,6 +39,7 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
 sys.path.insert(0, str(HERE.parents[1]))
 
 from mxwave_b200 import synthetic as syn  # noqa: E402
@@ -93,10 +100,17 @@ def edge_blocks() -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference MxWave checkout")
     ap.add_argument("--skip-configs", action="store_true")
+    ap.add_argument("--only-layers", action="store_true",
+                    help="only (re)generate the decoder-layer and expert-stack fixtures (configs 4 and 5)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
+    if args.only_layers:
+        import layer_golden
+
+        layer_golden.main(HERE)
+        return
     import torch
     from mxwave import calibration as ref_cal
     from mxwave import checkpoint as ref_ckpt

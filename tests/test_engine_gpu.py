@@ -173,3 +173,89 @@ def test_sequential_calibration_matches_reference(tmp_path, cuda_device) -> None
         for name in targets:
             torch.testing.assert_close(got.statistics[objective][name], want.statistics[objective][name],
                                        rtol=1e-5, atol=1e-6)
+
+
+# ------------------------------------------------ engine chunk stream
+
+
+def _engine_chunks(engine, shard, info, cfg, gamma=None, hessian=None):
+    out, err = [], None
+    try:
+        for start, stop, p, s in engine._quantized_chunks(shard, info, cfg, gamma, hessian):
+            out.append((start, stop, p.cpu().clone(), s.cpu().clone(), p.device.type))
+    except ValueError as exc:
+        err = str(exc)
+    return out, err
+
+
+def test_engine_stream_chunks_match_reference_loop(tmp_path, cuda_device) -> None:
+    """The installed _quantized_chunks yields the reference's chunks, bytes and NaN error."""
+    from safetensors.torch import save_file
+
+    engine = import_reference("mxwave.engine")
+    shard_mod = import_reference("mxwave.shard")
+    from mxwave_b200.install import install
+
+    bits = syn.det_dense_weight(1000, 1024, 21, outlier_fraction=0.01)
+    good = torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+    bad = good.clone()
+    bad[613, 77] = float("nan")
+    path = tmp_path / "w.safetensors"
+    save_file({"a.weight": good, "b.weight": bad, "c.weight": good[:, :992].contiguous()}, str(path))
+    shard = shard_mod.ShardFile(path=path, weight_map={})
+    infos = shard_mod.shard_tensor_info(shard)
+    gamma = torch.rand(1024) + 0.25
+    for name, kw in (("a.weight", {}), ("a.weight", {"gamma": gamma}), ("b.weight", {}), ("c.weight", {})):
+        base = dict(model_dir=tmp_path, output_dir=tmp_path / "o", policy="all-linear", verbose=False,
+                    tensor_row_chunk_size=96, tensor_chunk_max_elements=1 << 20)
+        cpu_cfg = engine.QuantizeConfig(device="cpu", **base)
+        want = _engine_chunks(engine, shard, infos[name], cpu_cfg, **kw)
+        handle = install()
+        try:
+            eng = sys.modules["mxwave.engine"]
+            gpu_cfg = eng.QuantizeConfig(device="cuda:0", **base)
+            dkw = {k: v.to(cuda_device) for k, v in kw.items()}
+            got = _engine_chunks(eng, shard, infos[name], gpu_cfg, **dkw)
+        finally:
+            handle.uninstall()
+        assert [(a, b) for a, b, *_ in got[0]] == [(a, b) for a, b, *_ in want[0]], name
+        assert got[1] == want[1], name
+        for (_, _, gp, gs, dev), (_, _, wp, ws, _) in zip(got[0], want[0]):
+            assert dev == "cpu"  # host chunks: the writer's .cpu() is a no-op
+            assert torch.equal(gp, wp) and torch.equal(gs, ws)
+    assert want[1] is not None and "rows [576, 672)" in want[1]
+
+
+def test_engine_stream_defers_to_a_patched_quantizer(tmp_path, cuda_device) -> None:
+    from safetensors.torch import save_file
+
+    import_reference("mxwave.engine")
+    shard_mod = import_reference("mxwave.shard")
+    from mxwave_b200.install import install
+
+    bits = syn.det_dense_weight(64, 256, 22)
+    path = tmp_path / "w.safetensors"
+    save_file({"a.weight": torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)}, str(path))
+    shard = shard_mod.ShardFile(path=path, weight_map={})
+    info = shard_mod.shard_tensor_info(shard)["a.weight"]
+    calls = []
+
+    def fake(chunk, **_kw):
+        calls.append(tuple(chunk.shape))
+        return (torch.zeros(chunk.shape[0], chunk.shape[1] // 2, dtype=torch.uint8, device=chunk.device),
+                torch.zeros(chunk.shape[0], chunk.shape[1] // 32, dtype=torch.uint8, device=chunk.device))
+
+    handle = install()
+    try:
+        eng = sys.modules["mxwave.engine"]
+        saved = eng.quantize_mxfp4
+        eng.quantize_mxfp4 = fake
+        try:
+            cfg = eng.QuantizeConfig(model_dir=tmp_path, output_dir=tmp_path / "o", device="cuda:0", verbose=False,
+                                     tensor_row_chunk_size=16, tensor_chunk_max_elements=1 << 20)
+            chunks = list(eng._quantized_chunks(shard, info, cfg, None, None))
+        finally:
+            eng.quantize_mxfp4 = saved
+    finally:
+        handle.uninstall()
+    assert len(chunks) == 4 and calls == [(16, 256)] * 4

@@ -77,3 +77,25 @@ def test_gguf_repack_is_byte_identical_to_reference(rows, cols, cuda_device) -> 
     got = repack_mxfp4_blocks(packed.to(cuda_device), scales.to(cuda_device))
     assert np.array_equal(got, ref.repack_mxfp4_blocks(packed, scales))
     assert np.array_equal(got, oracle.gguf_repack(packed.numpy(), scales.numpy()))
+
+
+def test_routed_finalize_is_bit_identical_on_the_same_accumulators(cuda_device) -> None:
+    """finalize's device pass rounds exactly like the reference's per-expert CPU loop."""
+    ref = import_reference("mxwave.routed_calibration")
+    experts, hidden, inter = 16, 384, 96
+    ids, weights = _routes(300, 2, experts - 3, 11)  # the last three experts never receive a route
+    g = torch.Generator().manual_seed(4)
+    want = ref.RoutedLayerMoments.create(experts, hidden, inter, torch.device("cpu"))
+    want.update_inputs(torch.randn(300, hidden, generator=g), ids, weights)
+    want.update_down(torch.randn(600, inter, generator=g), ids, weights)
+    want.input_squares[2].zero_()  # a routed expert with no energy stays uncalibrated
+    got = RoutedLayerMoments.create(experts, hidden, inter, cuda_device)
+    for field in ("input_squares", "down_squares", "route_mass", "observations", "down_observations"):
+        getattr(got, field).copy_(getattr(want, field))
+    stats_g, meta_g = got.finalize(5)
+    stats_w, meta_w = want.finalize(5)
+    assert meta_g == meta_w
+    assert list(stats_g) == list(stats_w)
+    for name in stats_w:
+        assert stats_g[name].device.type == "cpu" and stats_g[name].is_contiguous()
+        assert torch.equal(stats_g[name], stats_w[name]), name
