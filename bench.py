@@ -213,6 +213,12 @@ def run_ours(args) -> None:
     e2e = None if args.no_e2e else run_e2e(args, dev, world, rank)
     # ---- calibration: X^T X on the tensor cores (config 3's token set).
     xtx = None if args.no_xtx else run_xtx(args, dev, world, rank)
+    # ---- kernel timings of every objective and depth (rank 0 of one GPU).
+    sweep = run_sweep(args, dev) if (world == 1 and not args.no_sweep) else None
+    # ---- the decoder-layer, whole-checkpoint and engine workloads.
+    layer = run_decoder_layer(args, dev) if (world == 1 and not args.no_layers) else None
+    ckpt = None if args.no_layers else run_checkpoint_sweep(args, dev, world, rank)
+    engine = run_engine(args, dev) if (world == 1 and not args.no_layers) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -251,6 +257,10 @@ def run_ours(args) -> None:
         "e2e": e2e,
         "cpu_baseline": cpu,
         "calibration_xtx": xtx,
+        "quantize_sweep": sweep,
+        "decoder_layer": layer,
+        "checkpoint_sweep": ckpt,
+        "engine": engine,
         "gpu_launches": 6 * args.steps,  # moments, finalize, 2 x (quantize + rare-block fixup)
         "clocks": clocks.summary(),
     }
@@ -407,6 +417,378 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
     }
 
 
+def _flush_l2(buf) -> None:
+    buf.zero_()
+
+
+def _time_launches(fn, flush, reps: int) -> float:
+    """Median device time (ms) of fn() over reps launches, L2 flushed before each."""
+    import torch
+
+    times = []
+    for _ in range(reps):
+        flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def run_sweep(args, dev) -> dict:
+    """Quantize kernel timings per objective and depth on one 17408 x 5120 bf16 weight.
+
+    Every setting of the reference's quantize_mxfp4 that the workloads use:
+    unweighted (depth 1 and 4, percentile 100), gamma-weighted (depth 1, 4),
+    rtn, and the block-Hessian objective (depth 1, 4) with the 32x32 blocks of
+    the X^T X of 65536 heavy-channel tokens (damp 1e-6, absolute).  Each
+    number is the median of CUDA-event times around single launches (main
+    pass + rare-block pass) with L2 flushed before each; the roofline is the
+    algorithmic bytes (2.53125 B per weight + gamma / Hessian bytes) over that
+    time against the measured HBM copy bandwidth.
+    """
+    import torch
+
+    from mxwave_b200 import _lib, synthetic
+    from mxwave_b200.core import quantize_into
+
+    lib = _lib.load()
+    peak, peak_kind = _peaks()
+    w = synthetic.torch_dense_weight(INTER, HIDDEN, seed=31, device=dev, sigma=0.015)
+    x = synthetic.torch_activations(XTX_TOKENS, HIDDEN, seed=300, device=dev)
+    gram = torch.zeros(HIDDEN, HIDDEN, device=dev)
+    _lib.check(lib.mxw_accumulate_xtx(x.data_ptr(), XTX_TOKENS, HIDDEN, HIDDEN, gram.data_ptr(), HIDDEN, None,
+                                      torch.cuda.current_stream(dev).cuda_stream), "xtx")
+    hess = torch.empty(HIDDEN // 32, 32, 32, device=dev)
+    _lib.check(lib.mxw_finalize_block_hessian(gram.data_ptr(), 1, HIDDEN, HIDDEN, XTX_TOKENS, 1e-6,
+                                              _lib.MXW_DAMP_ABSOLUTE, hess.data_ptr(),
+                                              torch.cuda.current_stream(dev).cuda_stream), "finalize")
+    del x, gram
+    xs = synthetic.torch_activations(TOKENS, HIDDEN, seed=2, device=dev).float()
+    gamma = xs.square().mean(0).sqrt()
+    del xs
+    pk = torch.empty(INTER, HIDDEN // 2, dtype=torch.uint8, device=dev)
+    sc = torch.empty(INTER, HIDDEN // 32, dtype=torch.uint8, device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    settings = [
+        ("unweighted_d1", {}, 0), ("unweighted_d4", {"mse_clip_depth": 4}, 0),
+        ("unweighted_pct100_d1", {"scale_percentile": 100.0}, 0),
+        ("gamma_d1", {"gamma": gamma}, HIDDEN * 4), ("gamma_d4", {"gamma": gamma, "mse_clip_depth": 4}, HIDDEN * 4),
+        ("rtn", {"method": "rtn"}, 0),
+        ("hessian_d1", {"hessian": hess}, HIDDEN * 128), ("hessian_d4", {"hessian": hess, "mse_clip_depth": 4},
+                                                          HIDDEN * 128),
+    ]
+    out = {}
+    for name, kw, extra in settings:
+        def launch(kw=kw) -> None:
+            flags.zero_()
+            quantize_into(w, pk, sc, flags=flags, **kw)
+
+        for _ in range(3):
+            launch()
+        ms = _time_launches(launch, lambda: _flush_l2(flush), 9)
+        nbytes = INTER * HIDDEN * BYTES_PER_ELEM + extra
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 1), "algorithmic_GBps": round(gbs, 1), "frac": round(gbs / peak, 4),
+                     "bf16_weight_GBps": round(INTER * HIDDEN * 2 / (ms * 1e-3) / 1e9, 1)}
+    return {"workload": f"one {INTER} x {HIDDEN} bf16 weight per setting, pct {PCT} unless stated; Hessian blocks "
+                        f"from the X^T X of {XTX_TOKENS} heavy-channel tokens",
+            "peak_GBps": peak, "peak_kind": f"{peak_kind} copy bandwidth", "l2": "flushed before every launch",
+            "timing": "median of 9 single launches (main + rare-block pass), CUDA events", "settings": out}
+
+
+LAYER_LINEARS = (("self_attn.q_proj", 5120), ("self_attn.k_proj", 5120), ("self_attn.v_proj", 5120),
+                 ("self_attn.o_proj", 5120), ("mlp.gate_proj", 5120), ("mlp.up_proj", 5120),
+                 ("mlp.down_proj", 17408))
+
+
+def run_decoder_layer(args, dev) -> dict:
+    """Decoder-layer workload: layer-streamed calibration, then all seven linears quantized.
+
+    A random-init Qwen3.5 decoder layer (hidden 5120, gated q_proj, GQA 40/8 of
+    128, SwiGLU 17408, vocabulary 151936) in a safetensors checkpoint; 128
+    sequences x 2048 uniformly random token ids.  Calibration is
+    mxwave_b200.calibration_stream.calibrate_decoder_sequentially (bf16, rms +
+    block-Hessian statistics of every linear input, hidden states kept in
+    HBM), timed wall-clock from checkpoint to finalized statistics.  Then the
+    seven linears are quantized from HBM with their block Hessians and, as a
+    second pass, their rms gammas (depth 1), timed with CUDA events.
+    """
+    import tempfile
+
+    import torch
+    from safetensors import safe_open
+
+    from mxwave_b200 import synthetic
+    from mxwave_b200.calibration_stream import calibrate_decoder_sequentially
+    from mxwave_b200.core import quantize_into
+
+    _reference_importable()
+    cfg = synthetic.decoder_config(layers=1)
+    seqs, length = 128, 2048
+    g = torch.Generator().manual_seed(44)
+    ids = torch.randint(0, cfg.vocab_size, (seqs, length), generator=g).tolist()
+    targets = {f"model.layers.0.{n}.weight": w for n, w in LAYER_LINEARS}
+    objectives = ("rms", "block-hessian")
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / "model.safetensors"
+        files = synthetic.write_decoder_checkpoint(path, cfg, seed=4000, device=dev)
+        kw = dict(device=dev, dtype=torch.bfloat16, batch_size=16, hessian_damp=1e-6)
+        calibrate_decoder_sequentially(synthetic.meta_decoder(cfg), targets, objectives, ids[:16], files, **kw)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        res = calibrate_decoder_sequentially(synthetic.meta_decoder(cfg), targets, objectives, ids, files, **kw)
+        torch.cuda.synchronize(dev)
+        cal_s = time.perf_counter() - t0
+        with safe_open(str(path), framework="pt", device=str(dev)) as f:
+            weights = {n: f.get_tensor(n) for n in targets}
+    peak, peak_kind = _peaks()
+    out = {}
+    elems = sum(w.numel() for w in weights.values())
+    for objective, key in (("block-hessian", "hessian"), ("rms", "gamma")):
+        stats = {n: res.statistics[objective][n].to(dev) for n in targets}
+        bufs = {n: (torch.empty(w.shape[0], w.shape[1] // 2, dtype=torch.uint8, device=dev),
+                    torch.empty(w.shape[0], w.shape[1] // 32, dtype=torch.uint8, device=dev))
+                for n, w in weights.items()}
+
+        def launch() -> None:
+            for n, w in weights.items():
+                quantize_into(w, bufs[n][0], bufs[n][1], mse_clip_depth=1, **{key: stats[n]})
+
+        launch()
+        reps = 5
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            launch()
+        b.record()
+        b.synchronize()
+        ms = a.elapsed_time(b) / reps
+        nbytes = elems * BYTES_PER_ELEM + sum(s.numel() * 4 for s in stats.values())
+        out[f"{objective}_d1"] = {"ms_per_layer": round(ms, 3),
+                                  "bf16_weight_GBps": round(elems * 2 / (ms * 1e-3) / 1e9, 1),
+                                  "roofline_frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)}
+    tokens = seqs * length
+    return {
+        "workload": "random-init Qwen3.5 decoder layer (hidden 5120, GQA 40/8 x 128, gated q, SwiGLU 17408, "
+                    "vocab 151936), 128 x 2048 random token ids; rms + block-Hessian statistics of all 7 linear "
+                    "inputs, then all 7 linears quantized (depth 1)",
+        "calibration": {"tokens": tokens, "seconds": round(cal_s, 3), "tokens_per_s": round(tokens / cal_s, 1),
+                        "timing": "wall clock, checkpoint to finalized statistics, one layer"},
+        "quantize": out,
+        "weight_elements_per_layer": elems,
+        "peak_kind": f"{peak_kind} copy bandwidth",
+    }
+
+
+def _reference_importable() -> None:
+    ref = ROOT / "baseline" / "_ref"
+    if (ref / "mxwave").exists() and str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+
+
+def _h2d_bandwidth(dev) -> float:
+    """Pinned host -> device copy bandwidth (GB/s) of one 1 GiB copy, best of 3."""
+    import torch
+
+    src = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        b.synchronize()
+        best = max(best, (1 << 30) / (a.elapsed_time(b) * 1e-3) / 1e9)
+    return best
+
+
+def run_checkpoint_sweep(args, dev, world: int, rank: int) -> dict:
+    """Whole-checkpoint workload (a stated subset): host-pinned layers + the MoE expert stack.
+
+    4 decoder layers of the decoder-layer shape (7 linears each) and 128 routed
+    experts (gate/up 768 x 2048, down 2048 x 768) live in pinned host memory
+    and stream through ChunkStreamer (H2D / quantize / D2H on three streams)
+    with block-Hessian weighting at depth 1 (one synthetic Hessian per input
+    width).  Tensors are dealt round-robin over the ranks.  Reported: the
+    whole-job bf16 weight rate, its fraction of the measured pinned H2D link
+    bandwidth, and the kernel-only HBM fraction (the same quantize launches
+    with the weights resident in HBM).
+    """
+    import torch
+
+    from mxwave_b200 import synthetic
+    from mxwave_b200.core import compute_block_hessian, quantize_into
+    from mxwave_b200.streamer import ChunkStreamer
+
+    layers, experts = 4, 128
+    shapes = []
+    for layer in range(layers):
+        for n, k in LAYER_LINEARS:
+            rows = {"self_attn.q_proj": 10240, "self_attn.k_proj": 1024, "self_attn.v_proj": 1024,
+                    "self_attn.o_proj": 5120, "mlp.gate_proj": 17408, "mlp.up_proj": 17408,
+                    "mlp.down_proj": 5120}[n]
+            shapes.append((rows, k))
+    for _ in range(experts):
+        shapes += [(768, 2048), (768, 2048), (2048, 768)]
+    mine = [(i, s) for i, s in enumerate(shapes) if i % world == rank]
+    hess = {k: compute_block_hessian(synthetic.torch_activations(8192, k, seed=600 + k, device=dev))
+            for k in sorted({k for _, k in shapes})}
+    host = []
+    for i, (r, k) in mine:
+        w = synthetic.torch_dense_weight(r, k, seed=9000 + i, device=dev, outlier_fraction=0.0)
+        host.append((w.cpu().pin_memory(), k))
+    outs = [(torch.empty(w.shape[0], w.shape[1] // 2, dtype=torch.uint8).pin_memory(),
+             torch.empty(w.shape[0], w.shape[1] // 32, dtype=torch.uint8).pin_memory()) for w, _ in host]
+    link = _h2d_bandwidth(dev)
+    streamer = ChunkStreamer(dev)
+
+    def sweep() -> None:
+        for (w, k), (p, s) in zip(host, outs):
+            streamer.quantize(w, p, s, hessian=hess[k], mse_clip_depth=1)
+        streamer.finish()
+
+    sweep()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    sweep()
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b)
+    # Kernel-only: the same launches with each weight resident in HBM.
+    k_ms = 0.0
+    for w, k in host:
+        wd = w.to(dev)
+        pk = torch.empty(wd.shape[0], wd.shape[1] // 2, dtype=torch.uint8, device=dev)
+        sc = torch.empty(wd.shape[0], wd.shape[1] // 32, dtype=torch.uint8, device=dev)
+        quantize_into(wd, pk, sc, hessian=hess[k], mse_clip_depth=1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        quantize_into(wd, pk, sc, hessian=hess[k], mse_clip_depth=1)
+        e1.record()
+        e1.synchronize()
+        k_ms += e0.elapsed_time(e1)
+    elems_local = sum(w.numel() for w, _ in host)
+    elems_total = sum(r * k for r, k in shapes)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms, k_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, k_ms = float(t[0]), float(t[1])
+    peak, peak_kind = _peaks()
+    h2d_rate = elems_local * 2 / (ms * 1e-3) / 1e9
+    return {
+        "workload": f"{layers} decoder layers (7 linears of the decoder-layer shape) + {experts} experts "
+                    "(gate/up 768x2048, down 2048x768) bf16 in pinned host memory, block-Hessian depth 1, "
+                    f"tensors round-robin over {world} GPU(s)",
+        "subset": "4 of the 64 layers and one MoE layer of the whole-checkpoint workload",
+        "value": round(elems_total * 2 / (ms * 1e-3) / 1e9, 2),
+        "unit": "GB/s bf16 weight (whole job)",
+        "ms": round(ms, 2),
+        "weight_elements": elems_total,
+        "link": {"h2d_GBps_measured": round(link, 1), "h2d_GBps_achieved_per_gpu": round(h2d_rate, 1),
+                 "frac": round(h2d_rate / link, 4),
+                 "bytes_per_gpu": int(elems_local * 2 + elems_local * (0.5 + 1 / 32))},
+        "kernel_only": {"ms_per_gpu": round(k_ms, 2),
+                        "hbm_frac": round(elems_local * BYTES_PER_ELEM / (k_ms * 1e-3) / 1e9 / peak, 4),
+                        "peak_kind": f"{peak_kind} copy bandwidth"},
+    }
+
+
+def run_engine(args, dev) -> dict:
+    """mxwave.engine.quantize_model on a synthetic two-shard checkpoint, with and without this package.
+
+    The checkpoint holds two decoder layers of the decoder-layer shape (seven
+    linears each, bf16) plus their norms.  The reference engine runs on the
+    GPU twice: with its own torch implementation of the hot path, and with
+    this package installed (quantizer, chunk stream, SQNR off).  Wall clock of
+    quantize_model (planning, shard writing and fsync included); the output
+    shards of the two runs are compared byte for byte.
+    """
+    import hashlib
+    import tempfile
+
+    import torch
+    from safetensors.torch import save_file
+
+    from mxwave_b200 import synthetic
+
+    _reference_importable()
+    try:
+        import mxwave.engine as engine
+    except ImportError:
+        return {"unavailable": "reference package not installed in baseline/_ref"}
+    from mxwave_b200.install import install
+
+    shapes = {"self_attn.q_proj": (10240, 5120), "self_attn.k_proj": (1024, 5120), "self_attn.v_proj": (1024, 5120),
+              "self_attn.o_proj": (5120, 5120), "mlp.gate_proj": (17408, 5120), "mlp.up_proj": (17408, 5120),
+              "mlp.down_proj": (5120, 17408)}
+    with tempfile.TemporaryDirectory() as tmp:
+        model = Path(tmp) / "model"
+        model.mkdir()
+        weight_map = {}
+        elems = 0
+        for layer in range(2):
+            shard = {}
+            for i, (n, (r, k)) in enumerate(shapes.items()):
+                name = f"model.layers.{layer}.{n}.weight"
+                shard[name] = synthetic.torch_dense_weight(r, k, seed=5000 + 10 * layer + i, device=dev).cpu()
+                elems += r * k
+            shard[f"model.layers.{layer}.input_layernorm.weight"] = torch.ones(5120, dtype=torch.bfloat16)
+            fname = f"model-{layer + 1:05d}-of-00002.safetensors"
+            save_file(shard, str(model / fname))
+            weight_map.update({k: fname for k in shard})
+        (model / "model.safetensors.index.json").write_text(json.dumps({"metadata": {}, "weight_map": weight_map}))
+        (model / "config.json").write_text(json.dumps({"model_type": "test"}))
+        (model / "tokenizer.json").write_text('{"version":"1.0"}')
+        common = dict(model_dir=model, policy="all-linear", verbose=False, device=str(dev))
+
+        def run(out: Path) -> float:
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            engine_mod = sys.modules["mxwave.engine"]
+            engine_mod.quantize_model(engine_mod.QuantizeConfig(output_dir=out, **common))
+            torch.cuda.synchronize(dev)
+            return time.perf_counter() - t0
+
+        def digest(out: Path) -> str:
+            h = hashlib.sha256()
+            for f in sorted(out.glob("*.safetensors")):
+                h.update(f.read_bytes())
+            return h.hexdigest()
+
+        ref_s = run(Path(tmp) / "ref")
+        handle = install()
+        try:
+            run(Path(tmp) / "warm")
+            ours_s = run(Path(tmp) / "ours")
+        finally:
+            handle.uninstall()
+        same = digest(Path(tmp) / "ref") == digest(Path(tmp) / "ours")
+    gb = elems * 2 / 1e9
+    return {
+        "workload": "mxwave.engine.quantize_model, 2 shards x 7 linears of the decoder-layer shape (bf16), "
+                    "policy all-linear, mse depth 1, one GPU",
+        "ours": {"seconds": round(ours_s, 3), "bf16_weight_GBps": round(gb / ours_s, 2)},
+        "reference_on_gpu": {"seconds": round(ref_s, 3), "bf16_weight_GBps": round(gb / ref_s, 2),
+                             "path": "the reference's own torch quantize_mxfp4 and chunk loop on the same GPU"},
+        "speedup": round(ref_s / ours_s, 2),
+        "output_shards_identical": same,
+        "weight_elements": elems,
+    }
+
+
 # ---------------------------------------------------------- CPU reference
 
 
@@ -444,6 +826,65 @@ def cpu_baseline(seconds: float) -> dict:
             "sample": f"{N_WEIGHTS} x {rows} rows x {HIDDEN} of the workload's weights ({dt:.1f} s)"}
 
 
+def _cpu_model() -> str | None:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def reference_python(seconds: float) -> dict:
+    """The reference's own Python (baseline/_ref) on the host cores: a bounded row sample.
+
+    mxwave.checkpoint.iter_quantized_row_chunks + mxwave.core.quantize_mxfp4
+    on CPU fp32 with torch using every host thread, on rows of the workload's
+    weights (gamma from the reference's own ActivationCollector).
+    """
+    import platform
+
+    import numpy as np
+    import torch
+
+    _reference_importable()
+    try:
+        from mxwave import calibration as ref_cal
+        from mxwave import checkpoint as ref_ckpt
+        from mxwave import core as ref_core
+    except ImportError:
+        return {"unavailable": "reference package not installed in baseline/_ref"}
+    from mxwave_b200 import synthetic
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    xb = synthetic.det_activations(1024, HIDDEN, seed=2)
+    col = ref_cal.ActivationCollector({"mlp.weight": HIDDEN}, ("rms",))
+    col.update("mlp.weight", torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16))
+    gamma = col.finalize()["rms"]["mlp.weight"]
+
+    def quantize(rows: int) -> float:
+        bits = synthetic.det_dense_weight(rows, HIDDEN, seed=20, sigma=0.015, outlier_fraction=0.0)
+        w = torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+        t0 = time.perf_counter()
+        for _ in ref_ckpt.iter_quantized_row_chunks(
+                lambda a, b: w[a:b], lambda c: ref_core.quantize_mxfp4(c, PCT, gamma=gamma, mse_clip_depth=DEPTH),
+                rows=rows, columns=HIDDEN, max_rows=1024, max_elements=ref_ckpt.DEFAULT_TENSOR_CHUNK_MAX_ELEMENTS,
+                name="w"):
+            pass
+        return time.perf_counter() - t0
+
+    probe = quantize(204)
+    rows = int(max(204, min(INTER, 204 * seconds / max(probe, 1e-3))))
+    dt = quantize(rows)
+    return {"value": round(rows * HIDDEN * 2 / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
+            "kind": "reference",
+            "cpu": _cpu_model() or platform.machine(),
+            "sample": f"{rows} rows x {HIDDEN} of one workload weight through the reference's chunk loop "
+                      f"({dt:.1f} s)"}
+
+
 def run_reference(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -452,12 +893,8 @@ def run_reference(args) -> None:
     from oracle import oracle
 
     threads = oracle.default_threads()
-    ws, gamma = _oracle_sample(256)
-    t0 = time.perf_counter()
-    oracle.quantize_mxfp4(ws[0], PCT, gamma=gamma, mse_clip_depth=DEPTH, threads=threads)
-    probe = time.perf_counter() - t0
-    # Each step quantizes a bounded row sample of both weights (~1.5 s of CPU work).
-    rows = int(max(32, min(INTER, 128 * 1.5 / max(probe, 1e-3))))
+    # The full workload per step: both 17408 x 5120 weights (about 1.3 s on 16 threads).
+    rows = INTER
     ws, gamma = _oracle_sample(rows)
 
     def step() -> None:
@@ -472,7 +909,8 @@ def run_reference(args) -> None:
     dt = time.perf_counter() - t0
     elems = N_WEIGHTS * rows * HIDDEN
     value = elems * 2 * args.steps / dt / 1e9
-    sample = f"{N_WEIGHTS} x {rows} rows x {HIDDEN} per step of the workload's weights"
+    sample = f"the whole workload: {N_WEIGHTS} x {rows} rows x {HIDDEN} per step"
+    py = None if args.no_reference_python else reference_python(args.cpu_seconds)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -490,6 +928,7 @@ def run_reference(args) -> None:
         "config": {"workload": WORKLOAD, "sample": sample},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
+        "reference_python": py,
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
@@ -507,6 +946,11 @@ def main() -> None:
     ap.add_argument("--no-xtx", action="store_true", help="skip the X^T X calibration measurement")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--no-graph", action="store_true", help="launch the timed steps one kernel at a time")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the per-objective quantize kernel timings")
+    ap.add_argument("--no-reference-python", action="store_true",
+                    help="--impl reference: skip timing the reference's own Python beside the port")
+    ap.add_argument("--no-layers", action="store_true",
+                    help="skip the decoder-layer, whole-checkpoint and engine workloads")
     ap.add_argument("--traffic", type=float, default=QUANT_TRAFFIC_BYTES,
                     help="dram bytes per quantize launch from an ncu capture (recorded in the roofline)")
     args = ap.parse_args()

@@ -30,4 +30,10 @@ int make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* 
                        int64_t rows, int64_t row_bytes, int box_cols, int box_rows,
                        CUtensorMapSwizzle swizzle);
 
+// Diagonal 32x32 blocks of X^T X on the tensor cores (xtx.cu) for 2-byte
+// activations with cols % 128 == 0 and TMA-compatible layout; MXW_EUNSUPPORTED
+// when the input does not qualify.
+int accumulate_block_gram_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ld,
+                             float* gram_blocks, uint32_t* flags, cudaStream_t stream);
+
 }  // namespace mxw

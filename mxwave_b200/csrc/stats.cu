@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(kStatThreads, GRAM ? 2 : 3)
   constexpr int RB = 32 * StatElem<DT>::kBytes;  // bytes per tile row
   // Unswizzled TMA tiles need 128-byte aligned destinations.
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* smem = align_smem<128>(smem_raw);
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStatStages * kStatTileBytes);
   uint64_t* empty = full + kStatStages;
@@ -370,9 +370,20 @@ extern "C" int mxw_accumulate_activation_stats(const void* x, int dtype, int64_t
   P.sum_sq = sum_sq;
   P.gram_blocks = gram_blocks;
   P.flags = flags;
-  const bool moments = sum_abs || sum_sq;
-  const bool gram = gram_blocks != nullptr;
+  bool moments = sum_abs || sum_sq;
+  bool gram = gram_blocks != nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (gram) {
+    // The block Gram on the tensor cores when the input qualifies (2-byte
+    // activations, 128-channel strips, TMA layout); the moments, if asked
+    // for, then take the CUDA-core pass of their own.
+    const int rc = accumulate_block_gram_tc(x, dtype, tokens, cols, ld, gram_blocks, flags, s);
+    if (rc != MXW_EUNSUPPORTED) {
+      if (rc != MXW_OK || !moments) return rc;
+      gram = false;
+      P.gram_blocks = nullptr;
+    }
+  }
   switch (dtype) {
     case MXW_BF16:
       return launch_stats<MXW_BF16>(x, ld, P, moments, gram, s);

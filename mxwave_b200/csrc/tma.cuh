@@ -14,6 +14,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// A pointer into dynamic shared memory rounded up to ALIGN bytes.  It stays
+// derived from the __shared__ array by pointer arithmetic (no round trip
+// through an integer), so the compiler keeps treating it as shared memory and
+// emits shared loads and stores through it rather than generic ones.
+template <uint32_t ALIGN>
+__device__ __forceinline__ uint8_t* align_smem(uint8_t* smem_raw) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  return smem_raw + (((a + ALIGN - 1) & ~(ALIGN - 1)) - a);
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -30,9 +30,13 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "runtime.h"
 #include "tma.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace mxw {
 
@@ -200,7 +204,7 @@ __device__ __forceinline__ void add_tile_rows(float* gram, int64_t ldg, int64_t 
 __global__ void __launch_bounds__(kXtxThreads, 1)
     xtx_kernel(const __grid_constant__ CUtensorMap map, const XtxParams P) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = align_smem<1024>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kXtxStages * kXtxStageBytes);
   uint64_t* empty = full + kXtxStages;
   uint64_t* tfull = empty + kXtxStages;  // [2] accumulator buffer ready
@@ -389,6 +393,259 @@ static int64_t xtx_tiles(int64_t cols) {
   int64_t n = 0;
   for (int64_t by = 0; by < cols / kXtxBM; ++by) n += n_col_tiles - (by >> 1);
   return n;
+}
+
+// ------------------------------------------------ block-diagonal Gram
+//
+// The diagonal 32x32 blocks of X^T X (the reference's block Hessian,
+// mxwave/calibration.py:233-236) on the tensor cores.  A CTA owns one strip
+// of 128 channels (four 32-channel blocks) and one contiguous token slice.
+// Each stage is one TMA tile X[n0:n0+64, c0:c0+128]; it is both MMA operands
+// (A = B: the 128 x 128 tile X_s^T X_s, M = N = 128, K = 16 per instruction,
+// 4 per stage), accumulated in TMEM in chunks of 256 tokens (two 128-column
+// buffers).  Four epilogue warps read only the diagonal 32x32 sub-blocks
+// (warp quarter q: TMEM lanes 32q.., columns 32q..) and add each chunk into
+// round-to-nearest fp32 totals in registers, as the full X^T X kernel does.
+// The CTAs of one strip form a thread-block cluster; rank 0 sums the ranks'
+// totals over distributed shared memory in rank order and adds them into the
+// caller's blocks, so the result is deterministic.  The other three quarters
+// of each tile's MMA work are discarded: the tensor core has far more
+// throughput than this HBM-bound pass needs.
+
+constexpr int kBgStages = 8;
+constexpr int kBgStageBytes = 2 * kXtxBoxBytes;  // 64 tokens x 128 channels
+constexpr int kBgThreads = 6 * 32;               // producer, MMA, 4 epilogue warps
+constexpr uint32_t kBgTmemCols = 256;            // two 128 x 128 fp32 accumulators
+constexpr int kBgMaxSlices = 8;
+
+struct BgParams {
+  int64_t tokens, cols;
+  float* gram_blocks;
+  uint32_t* flags;
+};
+
+template <bool F16>
+__global__ void __launch_bounds__(kBgThreads, 1)
+    block_gram_tc_kernel(const __grid_constant__ CUtensorMap map, const BgParams P) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = align_smem<1024>(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBgStages * kBgStageBytes);
+  uint64_t* empty = full + kBgStages;
+  uint64_t* tfull = empty + kBgStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* fail = reinterpret_cast<int*>(tmem_slot + 1);
+  // This CTA's totals for the cluster fold: [quarter][lane][32] (16 KB), in
+  // stage 0 once the pipeline has drained (read by rank 0 over DSMEM).
+  float* part = reinterpret_cast<float*>(smem);
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned rank = cluster.block_rank();
+  const unsigned nrank = cluster.num_blocks();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * 128;
+  const int64_t n_kb = (P.tokens + kXtxBK - 1) / kXtxBK;
+  const int64_t kb_begin = n_kb * rank / nrank, kb_end = n_kb * (rank + 1) / nrank;
+  const int64_t n_chunks = (kb_end - kb_begin + kXtxChunkStages - 1) / kXtxChunkStages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBgStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *fail = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kBgTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  float total[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) total[k] = 0.0f;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&map);
+      bool ok = true;
+      int64_t i = 0;
+      for (int64_t kb = kb_begin; kb < kb_end; ++kb, ++i) {
+        const int s = static_cast<int>(i % kBgStages);
+        if (i >= kBgStages && !mbar_wait(&empty[s], static_cast<uint32_t>((i / kBgStages - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * kBgStageBytes;
+        mbar_arrive_expect_tx(&full[s], kBgStageBytes);
+        tma_load_2d(st, &map, &full[s], static_cast<int32_t>(c0), static_cast<int32_t>(kb * kXtxBK));
+        tma_load_2d(st + kXtxBoxBytes, &map, &full[s], static_cast<int32_t>(c0 + 64),
+                    static_cast<int32_t>(kb * kXtxBK));
+      }
+      for (int64_t j = (i > kBgStages ? i - kBgStages : 0); j < i; ++j)
+        if (!mbar_wait(&full[j % kBgStages], static_cast<uint32_t>((j / kBgStages) & 1))) ok = false;
+      if (!ok) atomicOr(fail, 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32_mn(128, 128) & (F16 ? ~((7u << 7) | (7u << 10)) : ~0u);
+      bool ok = true;
+      int64_t i = 0;
+      int64_t c = 0;
+      for (; c < n_chunks && ok; ++c) {
+        const int buf = static_cast<int>(c & 1);
+        if (c >= 2 && !mbar_wait(&tempty[buf], static_cast<uint32_t>((c / 2 - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(buf * 128);
+        const int64_t i_end = std::min<int64_t>((c + 1) * kXtxChunkStages, kb_end - kb_begin);
+        for (const int64_t first = i; i < i_end; ++i) {
+          const int s = static_cast<int>(i % kBgStages);
+          if (!mbar_wait(&full[s], static_cast<uint32_t>((i / kBgStages) & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * kBgStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kXtxBK / 16; ++kk) {
+            const uint64_t d = make_smem_desc_mn_sw128(base + kk * 2048, kXtxBoxBytes, 1024);
+            mma_bf16_f32(d_tmem, d, d, idesc, (i > first || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&tfull[buf]);
+      }
+      if (!ok) {
+        atomicOr(fail, 1);
+        for (; c < n_chunks; ++c) mma_commit(&tfull[c & 1]);
+      }
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lanes 32q.. (hardware rule) = block q of the strip
+    bool ok = true;
+    for (int64_t c = 0; c < n_chunks; ++c) {
+      const int buf = static_cast<int>(c & 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], static_cast<uint32_t>((c / 2) & 1)))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float v[32];
+      tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * 128 + 32 * q), v);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) total[k] = __fadd_rn(total[k], v[k]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+    if (!ok) atomicOr(fail, 1);
+  }
+  tc_fence_before();
+  __syncthreads();  // the pipeline has drained: stage memory is free for the totals
+  if (warp >= 2) {
+    float4* dst = reinterpret_cast<float4*>(part + ((warp & 3) * 32 + lane) * 32);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dst[k] = make_float4(total[4 * k], total[4 * k + 1], total[4 * k + 2], total[4 * k + 3]);
+  }
+  // Every thread of every CTA reaches both cluster barriers once (all waits above are bounded).
+  cluster_sync_all();
+  if (rank == 0 && warp >= 2) {
+    bool failed = false;
+    for (unsigned r = 0; r < nrank; ++r) failed |= *cluster.map_shared_rank(fail, r) != 0;
+    const int q = warp & 3;
+    if (failed) {
+      if (P.flags && lane == 0 && q == 0) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
+    } else {
+      float sum[32];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) sum[k] = total[k];
+      for (unsigned r = 1; r < nrank; ++r) {
+        const float4* src = reinterpret_cast<const float4*>(cluster.map_shared_rank(part, r) + (q * 32 + lane) * 32);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 o = src[k];
+          sum[4 * k] = __fadd_rn(sum[4 * k], o.x);
+          sum[4 * k + 1] = __fadd_rn(sum[4 * k + 1], o.y);
+          sum[4 * k + 2] = __fadd_rn(sum[4 * k + 2], o.z);
+          sum[4 * k + 3] = __fadd_rn(sum[4 * k + 3], o.w);
+        }
+      }
+      float4* g = reinterpret_cast<float4*>(P.gram_blocks + ((4 * blockIdx.x + q) * 32 + lane) * 32);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float4 o = g[k];
+        o.x = __fadd_rn(o.x, sum[4 * k]);
+        o.y = __fadd_rn(o.y, sum[4 * k + 1]);
+        o.z = __fadd_rn(o.z, sum[4 * k + 2]);
+        o.w = __fadd_rn(o.w, sum[4 * k + 3]);
+        g[k] = o;
+      }
+    }
+  }
+  cluster_sync_all();  // keep every rank's totals alive until rank 0 has read them
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kBgTmemCols);
+  }
+}
+
+// Token slices per strip: enough CTAs to cover the SMs, at least 16 K-blocks
+// (1024 tokens) per slice.
+static int bg_slices(int64_t strips, int64_t kblocks) {
+  int s = static_cast<int>(std::max<int64_t>(1, num_sms() / std::max<int64_t>(strips, 1)));
+  s = std::min<int>(s, kBgMaxSlices);
+  while (s > 1 && kblocks / s < 16) --s;
+  return s;
+}
+
+// Launches block_gram_tc_kernel for 2-byte activations whose layout suits TMA
+// and the 128-channel strips; returns MXW_EUNSUPPORTED otherwise (the caller
+// then uses the CUDA-core statistics kernel).
+int accumulate_block_gram_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ld,
+                             float* gram_blocks, uint32_t* flags, cudaStream_t stream) {
+  if ((dtype != MXW_BF16 && dtype != MXW_F16) || cols % 128 != 0 || ld % 8 != 0 ||
+      reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(gram_blocks) % 16 != 0 ||
+      tokens >= (int64_t(1) << 31) || cols >= (int64_t(1) << 31))
+    return MXW_EUNSUPPORTED;
+  const size_t smem = 1024 + kBgStages * kBgStageBytes + (2 * kBgStages + 4) * sizeof(uint64_t) + 16;
+  auto kern = dtype == MXW_F16 ? block_gram_tc_kernel<true> : block_gram_tc_kernel<false>;
+  const int rc = set_max_smem(reinterpret_cast<const void*>(kern), smem);
+  if (rc != MXW_OK) return rc;
+  const int64_t strips = cols / 128;
+  for (int64_t t0 = 0; t0 < tokens; t0 += kXtxMaxTokens) {
+    const int64_t n = std::min<int64_t>(kXtxMaxTokens, tokens - t0);
+    CUtensorMap map;
+    const CUtensorMapDataType dt = dtype == MXW_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    if (make_tensor_map_2d(&map, dt, static_cast<const uint16_t*>(x) + t0 * ld, cols, n, ld * 2, 64, kXtxBK,
+                           CU_TENSOR_MAP_SWIZZLE_128B) != MXW_OK)
+      return MXW_ECUDA;
+    BgParams P{n, cols, gram_blocks, flags};
+    const int S = bg_slices(strips, (n + kXtxBK - 1) / kXtxBK);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(strips), static_cast<unsigned>(S), 1);
+    cfg.blockDim = dim3(kBgThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = static_cast<unsigned>(S);
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, map, P);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    const int st = check_launch();
+    if (st != MXW_OK) return st;
+  }
+  return MXW_OK;
 }
 
 }  // namespace mxw

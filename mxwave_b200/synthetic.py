@@ -182,14 +182,63 @@ def torch_activations(tokens: int, cols: int, seed: int, device):
     return x.to(torch.bfloat16)
 
 
+# Decoder layer of the calibration workload: hidden 5120, 40 query / 8 KV heads
+# of 128 (gated q_proj: 40 * 128 * 2 outputs), SwiGLU intermediate 17408.
+DECODER_SHAPE = {"hidden": 5120, "heads": 40, "kv_heads": 8, "head_dim": 128, "intermediate": 17408,
+                 "vocab": 151936}
+
+
+def decoder_config(layers: int, vocab: int | None = None):
+    """transformers Qwen3.5 text config of the calibration workload's decoder (full attention)."""
+    from transformers.models.qwen3_5 import configuration_qwen3_5 as qc
+
+    d = DECODER_SHAPE
+    return qc.Qwen3_5TextConfig(hidden_size=d["hidden"], num_attention_heads=d["heads"],
+                                num_key_value_heads=d["kv_heads"], head_dim=d["head_dim"],
+                                intermediate_size=d["intermediate"], num_hidden_layers=layers,
+                                vocab_size=vocab or d["vocab"], layer_types=["full_attention"] * layers)
+
+
+def meta_decoder(config):
+    """The model skeleton on the meta device (weights come from the checkpoint)."""
+    import torch
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as qm
+
+    with torch.device("meta"):
+        return qm.Qwen3_5ForCausalLM(config)
+
+
+def write_decoder_checkpoint(path, config, seed: int, device) -> dict:
+    """Random-init weights of `config` (N(0, 0.02^2) matrices, zero RMSNorm offsets) as one
+    safetensors file; returns the tensor name -> path map calibration takes."""
+    import torch
+    from safetensors.torch import save_file
+
+    tensors = {}
+    for i, (name, param) in enumerate(meta_decoder(config).named_parameters()):
+        if name == "lm_head.weight":
+            continue
+        if param.ndim == 2:
+            tensors[name] = torch_dense_weight(*param.shape, seed=seed + i, device=device,
+                                               outlier_fraction=0.0).cpu()
+        else:
+            tensors[name] = torch.zeros(tuple(param.shape), dtype=torch.bfloat16)
+    save_file(tensors, str(path))
+    return {k: path for k in tensors}
+
+
 __all__ = [
+    "DECODER_SHAPE",
     "bf16_bits_to_f32",
+    "decoder_config",
     "det_activations",
     "det_channel_scales",
     "det_dense_weight",
     "det_normal",
     "det_uniform",
     "f32_to_bf16_bits",
+    "meta_decoder",
     "torch_activations",
     "torch_dense_weight",
+    "write_decoder_checkpoint",
 ]

@@ -62,6 +62,32 @@ def test_moments_and_block_gram(tokens, cols, dtype, cuda_device) -> None:
     assert _gram_err(g.cpu().numpy(), oracle.block_gram(xf)) < RTOL
 
 
+# Widths that are multiples of 128 with 2-byte activations take the tensor-core
+# block Gram (xtx.cu block_gram_tc_kernel): one to eight token slices per
+# 128-channel strip, and more than one launch past 262,144 tokens.
+TC_SIZES = [(1, 128), (63, 256), (300, 384), (4097, 640), (70001, 256), (262200, 128)]
+
+
+@pytest.mark.parametrize("tokens,cols", TC_SIZES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_block_gram_on_tensor_cores(tokens, cols, dtype, cuda_device) -> None:
+    lib = _lib.load()
+    x, xf = _x(tokens, cols, 3 * tokens + cols, cuda_device, dtype)
+    code = _lib.MXW_BF16 if dtype == torch.bfloat16 else _lib.MXW_F16
+    ref = oracle.block_gram(xf)
+    grams = []
+    for _ in range(2):
+        g = torch.zeros(cols // 32, 32, 32, device=cuda_device)
+        s2 = torch.zeros(cols, device=cuda_device)
+        assert lib.mxw_accumulate_activation_stats(x.data_ptr(), code, tokens, cols, cols, None, s2.data_ptr(),
+                                                   g.data_ptr(), None, _stream(cuda_device)) == 0
+        torch.cuda.synchronize()
+        assert _gram_err(g.cpu().numpy(), ref) < RTOL
+        np.testing.assert_allclose(s2.cpu().numpy(), oracle.moments(xf)[1], rtol=RTOL)
+        grams.append(g.cpu())
+    assert torch.equal(grams[0], grams[1])  # deterministic run to run
+
+
 def test_accumulation_across_calls_and_ragged_width(cuda_device) -> None:
     lib = _lib.load()
     x, xf = _x(3000, 5120, 5, cuda_device)
