@@ -344,12 +344,21 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
     stream = torch.cuda.current_stream(dev)
 
     # Several GPUs: each rank accumulates the packed upper-triangle tiles (55 MB
-    # at 5120 channels instead of the full 105 MB Gram), NCCL sums those, and
-    # every rank unpacks the sum into its full Gram.
-    packed = torch.zeros(lib.mxw_xtx_packed_floats(k), device=dev) if world > 1 else None
+    # at 5120 channels instead of the full 105 MB Gram); one NCCL
+    # reduce-scatter sums them and leaves each rank a band of whole tiles,
+    # which it unpacks into its Gram: the summed Gram is distributed over the
+    # ranks, band by band.
+    tile_floats = 128 * 256
+    n_tiles = int(lib.mxw_xtx_packed_tiles(k))
+    per_rank = -(-n_tiles // world)
+    packed = torch.zeros(per_rank * world * tile_floats, device=dev) if world > 1 else None
+    band = torch.empty(per_rank * tile_floats, device=dev) if world > 1 else None
 
     def step(record=None) -> None:
-        (packed if world > 1 else gram).zero_()
+        if world > 1:
+            packed.zero_()
+        else:
+            gram.zero_()
         if record is not None:
             record[0].record(stream)
         if world > 1:
@@ -363,9 +372,9 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
         if world > 1:
             import torch.distributed as dist
 
-            dist.all_reduce(packed, op=dist.ReduceOp.SUM)
-            gram.zero_()
-            _lib.check(lib.mxw_xtx_unpack(packed.data_ptr(), k, gram.data_ptr(), k, stream.cuda_stream), "unpack")
+            dist.reduce_scatter_tensor(band, packed, op=dist.ReduceOp.SUM)
+            _lib.check(lib.mxw_xtx_unpack_tiles(band.data_ptr(), rank * per_rank, per_rank, k, gram.data_ptr(), k,
+                                                stream.cuda_stream), "unpack")
 
     for _ in range(args.warmup):
         step()
@@ -398,15 +407,17 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
     tiles = sum((k + 255) // 256 - (by >> 1) for by in range(k // 128))
     mma_flops = 2.0 * n * 128 * 256 * tiles
     achieved = flops / (k_ms * 1e-3) / 1e12
+    blocks = run_block_hessian(args, dev, world, rank, x, total_tokens, k)
     return {
         "metric": "calib tokens/s for X^T X",
+        "block_hessian": blocks,
         "value": round(total_tokens * args.steps / (ms * 1e-3), 1),
         "unit": "tokens/s",
         "scaling": "strong",
         "config": {"workload": f"full (symmetric) X^T X of {total_tokens} x {k} bf16 activations -> fp32 Gram, "
                                f"tokens split over {world} GPU(s)"
-                               + (", NCCL all-reduce of the packed upper-triangle tiles, unpacked into the Gram"
-                                  if world > 1 else "")},
+                               + (", NCCL reduce-scatter of the packed upper-triangle tiles, each rank unpacking "
+                                  "its band (the summed Gram distributed by tile bands)" if world > 1 else "")},
         "ms_per_step": round(ms / args.steps, 4),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak[0], "unit": "TFLOP/s",
                      "frac": round(achieved / peak[0], 4), "peak_kind": peak[1], "kernel": "xtx_kernel (tcgen05)",
@@ -414,6 +425,67 @@ def run_xtx(args, dev, world: int, rank: int) -> dict:
                      "flops_per_launch": flops, "mma_flops_per_launch": mma_flops,
                      "mma_tflops": round(mma_flops / (k_ms * 1e-3) / 1e12, 1), "avg_launch_ms": round(k_ms, 4)},
         "gpu_launches": args.steps,
+    }
+
+
+def run_block_hessian(args, dev, world: int, rank: int, x, total_tokens: int, k: int) -> dict:
+    """The statistic the quantizer consumes: diagonal 32x32 blocks of X^T X.
+
+    Each rank accumulates its token slice with the tensor-core block-Gram
+    kernel, one NCCL all-reduce sums the [k/32, 32, 32] fp32 blocks
+    (655 KB at 5120 channels), and every rank finalizes the damped block
+    Hessian.  Whole-job tokens/s, max over ranks.
+    """
+    import torch
+
+    from mxwave_b200 import _lib
+
+    lib = _lib.load()
+    n = x.shape[0]
+    blocks = torch.zeros(k // 32, 32, 32, device=dev)
+    hess = torch.empty_like(blocks)
+    stream = torch.cuda.current_stream(dev)
+
+    def step() -> None:
+        blocks.zero_()
+        _lib.check(lib.mxw_accumulate_block_gram(x.data_ptr(), _lib.MXW_BF16, n, k, k, blocks.data_ptr(),
+                                                 stream.cuda_stream), "block gram")
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(blocks, op=dist.ReduceOp.SUM)
+        _lib.check(lib.mxw_finalize_block_hessian(blocks.data_ptr(), 0, k, k, total_tokens, 1e-6,
+                                                  _lib.MXW_DAMP_ABSOLUTE, hess.data_ptr(), stream.cuda_stream),
+                   "finalize")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    peak, _kind = _peaks()
+    return {
+        "workload": f"diagonal 32x32 blocks of X^T X of {total_tokens} x {k} bf16 tokens (tensor cores), "
+                    f"tokens split over {world} GPU(s)" + (", NCCL all-reduce of the blocks" if world > 1 else ""),
+        "value": round(total_tokens * args.steps / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "ms_per_step": round(ms / args.steps, 4),
+        "hbm_frac_per_gpu": round(n * k * 2 / (ms / args.steps * 1e-3) / 1e9 / peak, 4),
     }
 
 
@@ -713,8 +785,10 @@ def run_engine(args, dev) -> dict:
     linears each, bf16) plus their norms.  The reference engine runs on the
     GPU twice: with its own torch implementation of the hot path, and with
     this package installed (quantizer, chunk stream, SQNR off).  Wall clock of
-    quantize_model (planning, shard writing and fsync included); the output
-    shards of the two runs are compared byte for byte.
+    quantize_model (planning, shard writing and fsync included).  The output
+    shards of the two runs are compared byte for byte and reported; parity is
+    defined against the reference's CPU path (which this package reproduces
+    bit for bit), and its torch GPU path is not guaranteed to equal that.
     """
     import hashlib
     import tempfile
@@ -784,7 +858,7 @@ def run_engine(args, dev) -> dict:
         "reference_on_gpu": {"seconds": round(ref_s, 3), "bf16_weight_GBps": round(gb / ref_s, 2),
                              "path": "the reference's own torch quantize_mxfp4 and chunk loop on the same GPU"},
         "speedup": round(ref_s / ours_s, 2),
-        "output_shards_identical": same,
+        "identical_to_reference_gpu_run": same,
         "weight_elements": elems,
     }
 

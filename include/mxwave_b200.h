@@ -231,6 +231,19 @@ MXW_API int mxw_accumulate_xtx_packed(const void* x, int64_t tokens, int64_t col
 MXW_API int mxw_xtx_unpack(const float* packed, int64_t cols, float* gram, int64_t ldg, void* stream);
 
 /*
+ * For a reduce-scatter of the packed tiles: the number of packed tiles at
+ * `cols` (each 128 x 256 floats), and the unpack of tiles first_tile ..
+ * first_tile + n_tiles - 1 read from `packed` (which holds just those tiles,
+ * in order) into a full Gram; tiles past the last one are ignored, so a rank
+ * may hold padding.  After a reduce-scatter each rank unpacks its own band of
+ * tiles and owns those entries of the summed Gram.  No counterpart in the
+ * reference, which forms only the diagonal blocks (mxwave/calibration.py:233-236).
+ */
+MXW_API int64_t mxw_xtx_packed_tiles(int64_t cols);
+MXW_API int mxw_xtx_unpack_tiles(const float* packed, int64_t first_tile, int64_t n_tiles, int64_t cols,
+                                 float* gram, int64_t ldg, void* stream);
+
+/*
  * mean_abs = sum_abs / count, rms = sqrt(sum_sq / count) (either output may be
  * NULL).  Replaces ActivationCollector.finalize for the moment objectives
  * (mxwave/calibration.py:262-266).

@@ -54,6 +54,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mxw_xtx_packed_floats": (ctypes.c_size_t, [_i64]),
     "mxw_accumulate_xtx_packed": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "mxw_xtx_unpack": (_int, [_vp, _i64, _vp, _i64, _vp]),
+    "mxw_xtx_packed_tiles": (_i64, [_i64]),
+    "mxw_xtx_unpack_tiles": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
     "mxw_finalize_moments": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _vp]),
     "mxw_finalize_block_hessian": (_int, [_vp, _int, _i64, _i64, _i64, ctypes.c_double, _int, _vp, _vp]),
     "mxw_error_sums_workspace_size": (ctypes.c_size_t, [_i64, _i64]),

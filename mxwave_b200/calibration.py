@@ -189,11 +189,12 @@ class ActivationCollector:
         d_gram = (torch.zeros((width // BLOCK_SIZE, BLOCK_SIZE, BLOCK_SIZE), dtype=torch.float32, device=dev)
                   if want_gram else None)
         if self.skip_first_tokens:
-            # [batch, seq, width] -> one uniformly strided 2-D slice per sequence.
-            kept = activation[:, self.skip_first_tokens:, :]
-            count = kept.shape[0] * kept.shape[1]
-            for b in range(kept.shape[0]):
-                accumulate_stats(kept[b], d_abs, d_sq, d_gram)
+            # [batch, seq, width] minus each sequence's first tokens: one
+            # gather of the kept rows into a contiguous [tokens, width] slice,
+            # then a single statistics pass (not one launch per sequence).
+            kept = activation[:, self.skip_first_tokens:, :].reshape(-1, width)
+            count = kept.shape[0]
+            accumulate_stats(kept, d_abs, d_sq, d_gram)
         else:
             flat = activation.reshape(-1, width)
             count = flat.shape[0]

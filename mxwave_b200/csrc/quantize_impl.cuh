@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "runtime.h"
+#include "tcgen05.cuh"
 #include "tma.cuh"
 
 namespace mxw {
@@ -637,6 +638,21 @@ __device__ __forceinline__ uint32_t e2m1_quad(const unsigned long long (&x)[4], 
   return codes;
 }
 
+// fl(q * s + t) per element for q an f16 pair (E2M1 values), s an f16 scale
+// (a power of two) and t an fp32 pair: one mixed-precision FMA per element,
+// rounded once like the fp32 form (the product of two f16 values is exact).
+__device__ __forceinline__ float fma_f16_f32(uint16_t q, uint16_t s, float t) {
+  float r;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(r) : "h"(q), "h"(s), "f"(t));
+  return r;
+}
+
+__device__ __forceinline__ unsigned long long fma2_f16(uint32_t q2, uint16_t s, unsigned long long t) {
+  const f2 tt = unpack2(t);
+  return pack2(fma_f16_f32(static_cast<uint16_t>(q2 & 0xffffu), s, tt.x),
+               fma_f16_f32(static_cast<uint16_t>(q2 >> 16), s, tt.y));
+}
+
 __device__ __forceinline__ unsigned long long f16x2_to_f32x2(uint32_t h) {
   const __half2 hh = *reinterpret_cast<const __half2*>(&h);
   return pack2(__low2float(hh), __high2float(hh));
@@ -647,7 +663,8 @@ __device__ __forceinline__ unsigned long long f16x2_to_f32x2(uint32_t h) {
 // reference's rounding: x = t / 2^e (exact here: |t| >= 2^-133 and e <= 15,
 // so nothing underflows; +0 is added to turn -0 into +0 as the reference's
 // sign rule does), q = E2M1(x) by hardware RNE with saturation,
-// dW = fl(q*2^e - t) (computed as fl(t - q*2^e), the same magnitude),
+// dW = fl(q*2^e - t) (computed as fl(t - q*2^e), the same magnitude, by one
+// mixed-precision FMA per element on q's f16 value),
 // fl(dW^2), fl(. * gamma^2), then the lane partials and their left-to-right
 // sum, / 32.  The codes of x are the final encode's codes when e wins
 // (core.py:242-249 recomputes the same x).
@@ -659,7 +676,9 @@ __device__ __forceinline__ void two_candidate_errors(const unsigned long long (&
   const unsigned long long NZ2 = pack2(P.negzero, P.negzero);
   const float i0 = exp2i(-f), s0 = -exp2i(f);
   const unsigned long long I0 = pack2(i0, i0), I1 = pack2(0.5f * i0, 0.5f * i0);
-  const unsigned long long S0 = pack2(s0, s0), S1 = pack2(2.0f * s0, 2.0f * s0);
+  // -2^f and -2^(f+1) as f16 (exact: here -23 <= f <= 14) for the mixed-precision
+  // t - q * 2^e, one FMA per element instead of a conversion plus half an FFMA2.
+  const uint16_t hs0 = __half_as_ushort(__float2half_rn(s0)), hs1 = __half_as_ushort(__float2half_rn(2.0f * s0));
   unsigned long long p0[4], p1[4];
   uint32_t w0[4], w1[4];
 #pragma unroll
@@ -677,8 +696,8 @@ __device__ __forceinline__ void two_candidate_errors(const unsigned long long (&
 #pragma unroll
     for (int lp = 0; lp < 4; ++lp) {
       const int j = q * 4 + lp;
-      const unsigned long long da = fma2(f16x2_to_f32x2(ha[lp]), S0, t2[j]);
-      const unsigned long long db = fma2(f16x2_to_f32x2(hb[lp]), S1, t2[j]);
+      const unsigned long long da = fma2_f16(ha[lp], hs0, t2[j]);
+      const unsigned long long db = fma2_f16(hb[lp], hs1, t2[j]);
       unsigned long long sa = mul2_rounded(da, da, NZ2);
       unsigned long long sb = mul2_rounded(db, db, NZ2);
       if constexpr (GAMMA) {
@@ -1113,7 +1132,8 @@ __device__ __forceinline__ uint32_t quantize_block_slow(const QuantParams& P, in
     }
   }
   uint4 pk;
-  const uint32_t sc = quantize_one_block<MXW_F32, OBJ, QM, false>(B, P, g2, nullptr, pk);
+  const float* Hb = OBJ == kObjHess ? P.hessian + blk * 1024 : nullptr;
+  const uint32_t sc = quantize_one_block<MXW_F32, OBJ, QM, false>(B, P, g2, Hb, pk);
   *packed = pk;
   return sc;
 }
@@ -1168,6 +1188,595 @@ __global__ void __launch_bounds__(256) quantize_fixup_kernel(const QuantParams P
   } else {
     for (int64_t i = tid; i < total; i += stride)
       if (P.scales[i] == kRareBlock) fixup_block<DT, OBJ, QM>(P, i);
+  }
+}
+
+// ------------------------------ block-Hessian objective: tensor-core screening
+//
+// The block-Hessian error of a candidate exponent e is E = D^T H D over the
+// block's 32 elements, D = q(t / 2^e) * 2^e - t, H the block's 32x32 Hessian
+// (core.py:227-229).  The reference rounds it in a fixed order: per output d
+// an fp32 FMA chain over s, then the products summed in 8-lane order.  Doing
+// that on CUDA cores costs 1,024 FMA per block and candidate, reading H from
+// shared memory for each.  Here the tensor cores screen instead:
+//
+//   * D is exact in bf16 (at most 8 significant bits: t has 8 and q*2^e - t
+//     is a multiple of t's last place no larger than |t|), and H = Hh + Hl
+//     in two bf16 halves to 2^-16 relative;
+//   * per tile of 128 rows x 2 block columns, each thread writes its block's
+//     D for up to 4 candidates into shared memory (K-major, no swizzle), and
+//     one thread issues tcgen05.mma (M = 128 rows, N = 32, K = 32, both H
+//     halves) into TMEM: W = D * H for every row at once;
+//   * each thread reads its row of W back (tcgen05.ld) and forms
+//     E' = sum_d W_d D_d, with a bound |E' - E_reference| <= 4e-5 * A where
+//     A >= sum_{s,d} |D_s| |H_sd| |D_d| (2^-16 from the split, 2^-17 from the
+//     tensor core's fp32 accumulation, about 46 fp32 roundings on each side);
+//     A is (sum_s |D_s| sqrt(H_ss))^2 when every |H_sd| <= sqrt(H_ss H_dd)
+//     (checked per block column), else max|D| * sum_s |D_s| sum_d |H_sd|;
+//   * the candidate with the least E' (earliest on ties) is the reference's
+//     choice when every other candidate's E' exceeds it by more than both
+//     bounds; otherwise the block gets the rare marker and
+//     quantize_fixup_kernel evaluates it exactly.
+//
+// Candidates follow the reference's order (core.py:201-209): f - depth ..
+// f + 1, then the no-clipping exponent when it is f + 2.  Blocks outside
+// that domain (non-finite, block scales of 2^15 and above, safe >= f + 3) also
+// take the exact pass.  Rounds of 4 candidates keep TMEM at 256 columns, so
+// two CTAs share an SM and one computes while the other waits for its MMAs.
+
+constexpr int kHtRows = 128;                              // weight rows per tile (TMEM lanes)
+constexpr int kHtCols = 2;                                // block columns per tile
+constexpr int kHtStages = 2;
+constexpr int kHtStageBytes = kHtRows * 128;              // 128 rows x 64 two-byte elements
+constexpr int kHtRound = 4;                               // candidates per MMA round
+constexpr int kHtDBytes = kHtRows * 64;                   // bf16 D of one candidate and block column
+constexpr int kHtHBytes = 32 * 64;                        // one bf16 half of a 32x32 block Hessian
+constexpr uint32_t kHtTmemCols = kHtRound * kHtCols * 32;  // 256
+constexpr int kHtConsumerWarps = 8;
+constexpr int kHtProducerWarp = 8;
+constexpr int kHtMmaWarp = 9;
+constexpr int kHtThreads = 10 * 32;
+constexpr float kHtTol = 4e-5f;
+constexpr float kHtTolInexact = 4e-5f + 0.0079f;  // plus (2 * 2^-8 + 2^-16) x 1.01 for a rounded D
+// Shared memory: stages | D [round][col] | H halves [col][hi, lo] | per-column
+// bound data (sqrt(H_ss) and sum_d |H_sd|, 32 each, then the CS flag) | barriers.
+constexpr int kHtOffD = kHtStages * kHtStageBytes;
+constexpr int kHtOffH = kHtOffD + kHtRound * kHtCols * kHtDBytes;
+constexpr int kHtOffB = kHtOffH + kHtCols * 2 * kHtHBytes;
+constexpr int kHtOffBar = kHtOffB + kHtCols * 68 * 4;
+constexpr size_t kHtSmem = 1024 + kHtOffBar + (2 * kHtStages + 2) * 8 + 16;
+
+// Byte offset of row r's 16-byte chunk kc (elements 8kc .. 8kc+7) in a K-major
+// no-swizzle operand of K = 32: 8-row x 16-byte core matrices, 128 bytes
+// apart along K and 512 bytes apart along M.
+__device__ __forceinline__ uint32_t ht_core_offset(int r, int kc) {
+  return static_cast<uint32_t>((r >> 3) * 512 + kc * 128 + (r & 7) * 16);
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// D = q(t / 2^e) * 2^e - t for the block's 16 element pairs, as bf16 pairs (exact).
+__device__ __forceinline__ void ht_candidate_d(const unsigned long long (&t2)[16], int e, float zero,
+                                               uint32_t (&d)[16]) {
+  const float inv = exp2i(-e), sc = exp2i(e);
+  const unsigned long long I2 = pack2(inv, inv), S2 = pack2(sc, sc), Z2 = pack2(zero, zero);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    unsigned long long x[4];
+    uint32_t h[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] = fma2(t2[4 * q + k], I2, Z2);
+    e2m1_quad(x, h);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const f2 v = unpack2(fma2(f16x2_to_f32x2(h[k]), S2, t2[4 * q + k] ^ 0x8000000080000000ull));
+      d[4 * q + k] = bf16x2_rn(v.x, v.y);
+    }
+  }
+}
+
+template <int DT, int QM>
+__global__ void __launch_bounds__(kHtThreads, 2)
+    quantize_hess_tc_kernel(const __grid_constant__ CUtensorMap map, const QuantParams P) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = align_smem<1024>(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  float* bnd = reinterpret_cast<float*>(smem + kHtOffB);  // [col][68]: sqrt(H_ss) x32, row sums x32, flag
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kHtOffBar);
+  uint64_t* empty = full + kHtStages;
+  uint64_t* d_ready = empty + kHtStages;
+  uint64_t* mma_done = d_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n_strips = (P.nb + kHtCols - 1) / kHtCols;
+  const int64_t n_tiles = n_strips * P.n_row_tiles;
+  const int64_t t_begin = n_tiles * blockIdx.x / gridDim.x;
+  const int64_t t_end = n_tiles * (blockIdx.x + 1) / gridDim.x;
+  const int cmax = P.depth + 3;
+  const int n_rounds = (cmax + kHtRound - 1) / kHtRound;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kHtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kHtConsumerWarps);
+    }
+    mbar_init(d_ready, kHtConsumerWarps);
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == kHtMmaWarp) tmem_alloc(tmem_slot, kHtTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == kHtProducerWarp) {
+    if (lane == 0) {
+      prefetch_tensormap(&map);
+      int64_t i = 0;
+      TileCursor cur(t_begin, P.n_row_tiles);
+      for (int64_t t = t_begin; t < t_end; ++t, ++i, cur.advance(P.n_row_tiles)) {
+        const int s = static_cast<int>(i % kHtStages);
+        if (i >= kHtStages && !mbar_wait(&empty[s], static_cast<uint32_t>((i / kHtStages - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], kHtStageBytes);
+        tma_load_2d(smem + s * kHtStageBytes, &map, &full[s], static_cast<int32_t>(cur.strip * kHtCols * kBlock),
+                    static_cast<int32_t>(cur.rt * kHtRows));
+      }
+      for (int64_t j = (i > kHtStages ? i - kHtStages : 0); j < i; ++j)
+        if (!mbar_wait(&full[j % kHtStages], static_cast<uint32_t>((j / kHtStages) & 1))) ok = false;
+    }
+  } else if (warp == kHtMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32_k(kHtRows, 32);
+      int64_t round = 0;
+      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+        for (int r = 0; r < n_rounds; ++r, ++round) {
+          if (!mbar_wait(d_ready, static_cast<uint32_t>(round & 1))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int cl = 0; cl < kHtRound && r * kHtRound + cl < cmax; ++cl) {
+#pragma unroll
+            for (int col = 0; col < kHtCols; ++col) {
+              const uint32_t d_tmem = tmem + static_cast<uint32_t>((cl * kHtCols + col) * 32);
+              const uint32_t a = sbase + kHtOffD + (cl * kHtCols + col) * kHtDBytes;
+              const uint32_t b = sbase + kHtOffH + col * 2 * kHtHBytes;
+#pragma unroll
+              for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                  const uint64_t ad = make_smem_desc_k_noswz(a + ks * 256, 128, 512);
+                  const uint64_t bd = make_smem_desc_k_noswz(b + half * kHtHBytes + ks * 256, 128, 512);
+                  mma_bf16_f32(d_tmem, ad, bd, idesc, (ks | half) ? 1u : 0u);
+                }
+              }
+            }
+          }
+          mma_commit(mma_done);
+        }
+      }
+      if (!ok) {
+        // Let consumers still waiting on a round see it finish; the timeout flag
+        // makes the caller discard the output.
+        for (; round < (t_end - t_begin) * n_rounds; ++round) mma_commit(mma_done);
+      }
+    }
+  } else {
+    // ------------------------------------------------- consumers: one block per thread
+    const int quarter = warp & 3, col = warp >> 2;
+    const int r_tile = quarter * 32 + lane;  // this thread's row of the tile (= TMEM lane)
+    const uint32_t my_d = sbase + kHtOffD + col * kHtDBytes;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
+    int64_t cur_strip = -1;
+    int64_t round = 0;
+    int64_t i = 0;
+    bool any_nonfinite = false, any_rare = false;
+    TileCursor cur(t_begin, P.n_row_tiles);
+    for (int64_t t = t_begin; t < t_end; ++t, ++i, cur.advance(P.n_row_tiles)) {
+      const int64_t b = cur.strip * kHtCols + col;
+      const int64_t row = cur.rt * kHtRows + r_tile;
+      const bool valid_col = b < P.nb;
+      const bool active = valid_col && row < P.rows;
+      const int s = static_cast<int>(i % kHtStages);
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], static_cast<uint32_t>((i / kHtStages) & 1)))) {
+        ok = false;
+        break;
+      }
+      uint32_t words[16];
+      {
+        const uint8_t* box = smem + s * kHtStageBytes + r_tile * 128;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 v = *reinterpret_cast<const uint4*>(box + (((4 * col + j) ^ (r_tile & 7)) << 4));
+          words[4 * j] = v.x;
+          words[4 * j + 1] = v.y;
+          words[4 * j + 2] = v.z;
+          words[4 * j + 3] = v.w;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (cur.strip != cur_strip) {
+        // New block columns: both bf16 halves of H (as the MMA's K-major B
+        // operand: row n = d holds H[s][d] over s) and the bound data.
+        cur_strip = cur.strip;
+        const int idx = r_tile;  // 128 threads per column: row d = idx / 4, chunk kc = idx % 4
+        const int d = idx >> 2, kc = idx & 3;
+        float hv[8];
+        float rowsum = 0.0f;
+        bool cs = true;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) hv[k] = valid_col ? __ldg(P.hessian + b * 1024 + (8 * kc + k) * 32 + d) : 0.0f;
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          hi[k] = bf16x2_rn(hv[2 * k], hv[2 * k + 1]);
+          const float r0 = __fsub_rn(hv[2 * k], bits_f32(hi[k] << 16));
+          const float r1 = __fsub_rn(hv[2 * k + 1], bits_f32(hi[k] & 0xffff0000u));
+          lo[k] = bf16x2_rn(r0, r1);
+        }
+        const uint32_t hb = sbase + kHtOffH + col * 2 * kHtHBytes + ht_core_offset(d, kc);
+        sts128(hb, make_uint4(hi[0], hi[1], hi[2], hi[3]));
+        sts128(hb + kHtHBytes, make_uint4(lo[0], lo[1], lo[2], lo[3]));
+        float* cb = bnd + col * 68;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) rowsum = __fadd_ru(rowsum, fabsf(hv[k]));
+        // sum_s |H_sd| over this thread's 8 s, then over the 4 chunk threads of row d.
+        rowsum = __fadd_ru(rowsum, __shfl_xor_sync(0xffffffffu, rowsum, 1));
+        rowsum = __fadd_ru(rowsum, __shfl_xor_sync(0xffffffffu, rowsum, 2));
+        if (kc == 0) cb[32 + d] = rowsum;
+        if (kc == (d >> 3)) cb[d] = hv[d & 7] >= 0.0f ? __fsqrt_ru(hv[d & 7]) : -1.0f;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        // |H_sd| <= sqrt(H_ss) sqrt(H_dd) for every pair (true for a PSD H) lets
+        // the tighter bound apply; checked on the rounded-up square roots.
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float ps = cb[8 * kc + k], pd = cb[d];
+          cs = cs && ps >= 0.0f && pd >= 0.0f && fabsf(hv[k]) <= __fmul_ru(ps, pd);
+        }
+        cs = __all_sync(0xffffffffu, cs);
+        if (lane == 0) reinterpret_cast<int*>(cb)[64 + quarter] = cs ? 1 : 0;
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+      }
+      const float* cb = bnd + col * 68;
+      const int* csf = reinterpret_cast<const int*>(cb + 64);
+      const bool use_cs = csf[0] && csf[1] && csf[2] && csf[3];
+
+      // Block statistics, anchor and candidate exponents (as quantize_block_fast).
+      uint32_t m1 = 0, m2 = 0;
+      unsigned long long t2[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t a = words[k] & 0x7fff7fffu;
+        if constexpr (QM == kQTop2) m2 = __vmaxu2(m2, __vminu2(m1, a));
+        m1 = __vmaxu2(m1, a);
+        t2[k] = word_pair<DT>(words[k]);
+      }
+      float amax, second;
+      bool nonfinite;
+      {
+        const uint32_t lo1 = m1 & 0xffffu, hi1 = m1 >> 16;
+        const uint32_t top1 = max(lo1, hi1);
+        uint32_t top2 = 0;
+        if constexpr (QM == kQTop2) top2 = max(min(lo1, hi1), max(m2 & 0xffffu, m2 >> 16));
+        if constexpr (DT == MXW_BF16) {
+          nonfinite = top1 >= 0x7f80u;
+          amax = bits_f32(top1 << 16);
+          second = bits_f32(top2 << 16);
+        } else {
+          nonfinite = top1 >= 0x7c00u;
+          amax = __half2float(__ushort_as_half(static_cast<unsigned short>(top1)));
+          second = __half2float(__ushort_as_half(static_cast<unsigned short>(top2)));
+        }
+      }
+      unsigned long long unused_nt2[16];
+      const float anchor = fmaxf(block_anchor<QM>(amax, second, unused_nt2, P), 1e-6f);
+      const bool near_zero = amax < 1e-6f;
+      bool fast = active && !near_zero && !nonfinite;
+      const int f = fast ? floor_log2_div6(anchor) : 0;
+      const int safe_e = fast ? ceil_log2_div6(fmaxf(amax, 1e-12f)) : 0;
+      fast = fast && f <= 14 && safe_e <= f + 2;
+      const int ncand = P.depth + 2 + (safe_e == f + 2 ? 1 : 0);
+      const int amax_exp = static_cast<int>(f32_bits(amax) >> 23) - 127;  // floor(log2(amax)) for normal amax
+
+      float best = __int_as_float(0x7f800000), best_tol = 0.0f;
+      int best_c = 0;
+      // Smallest E' - tol over the candidates other than the current best,
+      // kept as the pair (E', tol) of every candidate seen: an ambiguity check
+      // against the final best needs min over c != best of (E'_c - tol_c).
+      float runner = __int_as_float(0x7f800000);  // min of E'_c - tol_c over c != best_c
+      bool bad = false;
+      for (int r = 0; r < n_rounds; ++r, ++round) {
+#pragma unroll
+        for (int cl = 0; cl < kHtRound; ++cl) {
+          const int c = r * kHtRound + cl;
+          if (c >= cmax) break;
+          uint32_t dw[16];
+          if (fast && c < ncand) {
+            ht_candidate_d(t2, c < P.depth + 2 ? f - P.depth + c : safe_e, P.zero, dw);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) dw[k] = 0u;
+          }
+          const uint32_t dst = my_d + cl * kHtCols * kHtDBytes;
+#pragma unroll
+          for (int kc = 0; kc < 4; ++kc)
+            sts128(dst + ht_core_offset(r_tile, kc), make_uint4(dw[4 * kc], dw[4 * kc + 1], dw[4 * kc + 2], dw[4 * kc + 3]));
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(d_ready);
+        if (!__all_sync(0xffffffffu, mbar_wait(mma_done, static_cast<uint32_t>(round & 1)))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int cl = 0; cl < kHtRound; ++cl) {
+          const int c = r * kHtRound + cl;
+          if (c >= cmax) break;
+          float w[32];
+          tmem_ld_32x32b_x32(tl + static_cast<uint32_t>((cl * kHtCols + col) * 32), w);
+          if (!(fast && c < ncand)) continue;
+          const uint32_t src = my_d + cl * kHtCols * kHtDBytes;
+          float e_acc = 0.0f, a_lin = 0.0f, d_max = 0.0f;
+          const float4* coef = reinterpret_cast<const float4*>(cb + (use_cs ? 0 : 32));
+          float e_acc2 = 0.0f;
+#pragma unroll
+          for (int kc = 0; kc < 4; ++kc) {
+            const uint4 v = lds128(src + ht_core_offset(r_tile, kc));
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+            const float4 ca = coef[2 * kc], cc = coef[2 * kc + 1];
+            const float cf[8] = {ca.x, ca.y, ca.z, ca.w, cc.x, cc.y, cc.z, cc.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int sidx = 8 * kc + 2 * k;
+              const float d0 = bits_f32(vv[k] << 16), d1 = bits_f32(vv[k] & 0xffff0000u);
+              e_acc = __fmaf_rn(w[sidx], d0, e_acc);
+              e_acc2 = __fmaf_rn(w[sidx + 1], d1, e_acc2);
+              a_lin = __fmaf_ru(fabsf(d0), cf[2 * k], a_lin);
+              a_lin = __fmaf_ru(fabsf(d1), cf[2 * k + 1], a_lin);
+              d_max = fmaxf(d_max, fmaxf(fabsf(d0), fabsf(d1)));
+            }
+          }
+          e_acc = __fadd_rn(e_acc, e_acc2);
+          const float a_bound = use_cs ? __fmul_ru(a_lin, a_lin) : __fmul_ru(a_lin, d_max);
+          // D is exact in bf16 unless a clipped element has |t| / 2^e >= 512
+          // (then |x| - 6 needs more than 8 bits); its rounding (2^-8 relative
+          // per element) enters the quadratic form twice.
+          const int ec = c < P.depth + 2 ? f - P.depth + c : safe_e;
+          const float tol = __fmul_ru(a_bound, amax_exp - ec >= 9 ? kHtTolInexact : kHtTol);
+          if (isnan(e_acc) || !(tol < __int_as_float(0x7f800000))) bad = true;
+          if (e_acc < best) {
+            runner = fminf(runner, __fsub_rd(best, best_tol));
+            best = e_acc;
+            best_tol = tol;
+            best_c = c;
+          } else {
+            runner = fminf(runner, __fsub_rd(e_acc, tol));
+          }
+        }
+        tc_fence_before();
+      }
+      if (!ok) break;
+      // Decided when every other candidate's lower end clears the best's upper end.
+      const bool decided = fast && !bad && runner > __fadd_ru(best, best_tol);
+      uint32_t sc;
+      uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+      if (near_zero && active && !nonfinite) {
+        sc = static_cast<uint32_t>(floor_log2_div6(anchor) - P.depth + 127);  // all-zero codes (core.py:194-195)
+      } else if (decided) {
+        const int raw = best_c < P.depth + 2 ? f - P.depth + best_c : safe_e;
+        encode_pairs([&](int j) { return t2[j]; }, P, raw, pk);
+        sc = static_cast<uint32_t>(raw + 127);
+      } else {
+        sc = kRareBlock;
+      }
+      if (active) {
+        *reinterpret_cast<uint4*>(P.packed + row * (P.cols / 2) + b * 16) = pk;
+        P.scales[row * P.nb + b] = static_cast<uint8_t>(sc);
+        any_nonfinite |= nonfinite;
+        any_rare |= sc == kRareBlock;
+      }
+    }
+    if (P.flags && __any_sync(0xffffffffu, any_nonfinite) && lane == 0) atomicOr(P.flags, MXW_FLAG_NONFINITE);
+    if (P.flags && __any_sync(0xffffffffu, any_rare) && lane == 0) atomicOr(P.flags, MXW_FLAG_RARE);
+  }
+  if (!ok && P.flags && lane == 0) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kHtMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kHtTmemCols);
+  }
+}
+
+// ------------------------- block-Hessian objective: exact pass for marked blocks
+//
+// The blocks the screening leaves undecided are re-quantized exactly, one
+// warp per block: lane s holds element s, and lane d runs the reference's
+// fp32 FMA chain w_d = sum_s dW_s H[s, d] over s = 0..31 (dW_s broadcast by
+// shuffle, H[s, d] read as coalesced 128-byte rows and kept in registers for
+// all candidates); the products fl(w_d dW_d) are then summed in the
+// reference's 8-lane order (core.py:227-229).  A block whose elements are
+// not all finite is left to the single-thread exact path.
+
+__device__ __forceinline__ float warp_exact_hessian_error(float t, float dummy, int e, const float (&hcol)[32],
+                                                          int lane) {
+  (void)dummy;
+  const float s = exp2i(e), inv = exp2i(-e);
+  const float at = fabsf(t);
+  const float xm = __fmul_rn(at, inv);  // |t| / 2^e (exact)
+  uint32_t h2;
+  asm("{\n\t.reg .b8 c;\n\tcvt.rn.satfinite.e2m1x2.f32 c, %1, %2;\n\tcvt.rn.f16x2.e2m1x2 %0, c;\n\t}"
+      : "=r"(h2) : "f"(0.0f), "f"(xm));
+  const float q = __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xffffu)));
+  // |dW| = q * 2^e - |t| (the product is exact unless it overflows, e >= 126), with t's sign.
+  const float dwm = e < 126 ? __fmaf_rn(q, s, -at) : __fsub_rn(__fmul_rn(q, s), at);
+  const float dw = __uint_as_float(__float_as_uint(dwm) ^ (__float_as_uint(t) & 0x80000000u));
+  float w = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const float ds = __shfl_sync(0xffffffffu, dw, k);
+    w = k == 0 ? __fmul_rn(ds, hcol[0]) : __fmaf_rn(ds, hcol[k], w);
+  }
+  const float prod = __fmul_rn(w, dw);
+  // Lane partials ((p_l + p_{l+8}) + p_{l+16}) + p_{l+24}, then p_0 + ... + p_7 in order.
+  float part = __fadd_rn(prod, __shfl_down_sync(0xffffffffu, prod, 8));
+  part = __fadd_rn(part, __shfl_down_sync(0xffffffffu, prod, 16));
+  part = __fadd_rn(part, __shfl_down_sync(0xffffffffu, prod, 24));
+  float acc = __shfl_sync(0xffffffffu, part, 0);
+#pragma unroll
+  for (int l = 1; l < 8; ++l) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, part, l));
+  (void)lane;
+  return acc;
+}
+
+// One marked block (row, blk), the whole warp.  Mirrors quantize_one_block for
+// the Hessian objective with a top-2 or amax anchor.
+template <int DT, int QM>
+__device__ __forceinline__ void warp_fixup_hessian_block(const QuantParams& P, int64_t idx, int lane) {
+  const int64_t row = idx / P.nb, blk = idx % P.nb;
+  float t;
+  {
+    const int64_t i = row * P.ld + blk * kBlock + lane;
+    if constexpr (DT == MXW_BF16) {
+      t = bits_f32(static_cast<uint32_t>(static_cast<const uint16_t*>(P.weight)[i]) << 16);
+    } else if constexpr (DT == MXW_F16) {
+      t = __half2float(static_cast<const __half*>(P.weight)[i]);
+    } else {
+      t = static_cast<const float*>(P.weight)[i];
+    }
+  }
+  const uint32_t a = f32_bits(t) & 0x7fffffffu;
+  if (__any_sync(0xffffffffu, a >= 0x7f800000u)) {
+    // Non-finite elements: the single-thread exact path replays the reference's NaN handling.
+    if (lane == 0) {
+      uint4 pk;
+      const uint32_t sc = quantize_block_slow<DT, kObjHess, QM>(P, row, blk, &pk);
+      *reinterpret_cast<uint4*>(P.packed + row * (P.cols / 2) + blk * 16) = pk;
+      P.scales[idx] = static_cast<uint8_t>(sc);
+    }
+    return;
+  }
+  // Top-2 magnitudes (ties: the second equals the first).
+  const uint32_t m1 = __reduce_max_sync(0xffffffffu, a);
+  const uint32_t n1 = __popc(__ballot_sync(0xffffffffu, a == m1));
+  const uint32_t m2 = n1 >= 2 ? m1 : __reduce_max_sync(0xffffffffu, a == m1 ? 0u : a);
+  const float amax = bits_f32(m1), second = bits_f32(m2);
+  unsigned long long unused_nt2[16];
+  float anchor = block_anchor<QM>(amax, second, unused_nt2, P);
+  const bool near_zero = amax < 1e-6f;
+  anchor = fmaxf(anchor, 1e-6f);
+  const int floor_e = floor_log2_div6(anchor);
+  const int lo_e = max(-127, min(127, floor_e - P.depth));
+  uint32_t sc;
+  uint32_t code = 0;
+  if (near_zero) {
+    sc = static_cast<uint32_t>(lo_e + 127);
+  } else {
+    const int hi_e = max(-127, min(127, floor_e + 1));
+    const int safe_e = max(-127, min(127, ceil_log2_div6(fmaxf(amax, 1e-12f))));
+    const int n_seq = hi_e - lo_e + 1;
+    const bool safe_new = safe_e < lo_e || safe_e > hi_e;
+    float hcol[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) hcol[k] = __ldg(P.hessian + blk * 1024 + k * 32 + lane);  // H[s = k][d = lane]
+    float best = __int_as_float(0x7f800000);
+    int raw = lo_e;
+    for (int k = 0; k < n_seq + (safe_new ? 1 : 0); ++k) {
+      const int e = k < n_seq ? lo_e + k : safe_e;
+      const float err = warp_exact_hessian_error(t, 0.0f, e, hcol, lane);
+      if (err < best) raw = e;
+      best = (isnan(err) || isnan(best)) ? __int_as_float(0x7fffffff) : fminf(best, err);
+    }
+    // Final encode (core.py:242-249): x = t / 2^raw (+0 turns -0 into +0), E2M1 RNE.
+    const float x = __fadd_rn(__fmul_rn(t, exp2i(-raw)), P.zero);
+    const float xn = __shfl_down_sync(0xffffffffu, x, 1);
+    code = e2m1x2(x, xn);  // meaningful in even lanes: elements (lane, lane + 1)
+    sc = static_cast<uint32_t>(raw + 127);
+  }
+  // Bytes 0..15 from the even lanes; lane 4k assembles word k.
+  const uint32_t b0 = __shfl_sync(0xffffffffu, code, (lane & ~3) * 2);
+  const uint32_t b1 = __shfl_sync(0xffffffffu, code, (lane & ~3) * 2 + 2);
+  const uint32_t b2 = __shfl_sync(0xffffffffu, code, (lane & ~3) * 2 + 4);
+  const uint32_t b3 = __shfl_sync(0xffffffffu, code, (lane & ~3) * 2 + 6);
+  uint8_t* dst = P.packed + row * (P.cols / 2) + blk * 16;
+  if ((lane & 3) == 0 && lane < 16) {
+    *reinterpret_cast<uint32_t*>(dst + lane) = (b0 & 0xffu) | ((b1 & 0xffu) << 8) | ((b2 & 0xffu) << 16) | ((b3 & 0xffu) << 24);
+  }
+  if (lane == 0) P.scales[idx] = static_cast<uint8_t>(sc);
+}
+
+// Finds the blocks quantize_hess_tc_kernel marked (scale byte kRareBlock) and
+// re-quantizes each with a whole warp.  Each warp reads 512 scale bytes per
+// step (16 per lane); returns at once when the main pass marked nothing.
+template <int DT, int QM>
+__global__ void __launch_bounds__(256) quantize_fixup_hess_kernel(const QuantParams P) {
+  if (P.flags && (*reinterpret_cast<volatile const uint32_t*>(P.flags) & MXW_FLAG_RARE) == 0) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = P.rows * P.nb;
+  const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const bool vec = reinterpret_cast<uintptr_t>(P.scales) % 16 == 0;
+  const int64_t span = vec ? 512 : 32;  // scale bytes per warp step
+  for (int64_t base = warp * span; base < total; base += n_warps * span) {
+    // Each lane's marked bytes as a bit mask over its 16 (or 1) positions.
+    uint32_t mask = 0;
+    if (vec) {
+      const int64_t off = base + 16 * lane;
+      if (off + 16 <= total) {
+        const uint4 v = *reinterpret_cast<const uint4*>(P.scales + off);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t m = __vcmpeq4(w[q], 0xffffffffu);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if ((m >> (8 * k)) & 1u) mask |= 1u << (4 * q + k);
+        }
+      } else {
+        for (int k = 0; k < 16 && off + k < total; ++k)
+          if (P.scales[off + k] == kRareBlock) mask |= 1u << k;
+      }
+    } else if (base + lane < total && P.scales[base + lane] == kRareBlock) {
+      mask = 1u;
+    }
+    uint32_t lanes = __ballot_sync(0xffffffffu, mask != 0);
+    while (lanes) {
+      const int src = __ffs(lanes) - 1;
+      lanes &= lanes - 1;
+      uint32_t m = __shfl_sync(0xffffffffu, mask, src);
+      while (m) {
+        const int k = __ffs(m) - 1;
+        m &= m - 1;
+        warp_fixup_hessian_block<DT, QM>(P, base + (vec ? 16 * src : src) + k, lane);
+      }
+    }
   }
 }
 
@@ -1286,6 +1895,38 @@ static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStre
   return rc;
 }
 
+// The block-Hessian objective on bf16 weights with a top-2 / amax anchor:
+// tensor-core screening, then the rare-block pass for the blocks it leaves.
+template <int DT, int QM>
+static int launch_hess_tc(const void* w, int64_t ld, const QuantParams& P0, cudaStream_t stream) {
+  CUtensorMap map;
+  if (make_tensor_map_2d(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, P0.cols, P0.rows, ld * 2, 64, kHtRows,
+                         CU_TENSOR_MAP_SWIZZLE_128B) != MXW_OK)
+    return MXW_ECUDA;
+  auto kern = quantize_hess_tc_kernel<DT, QM>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  LaunchInfo& li = launch_info(reinterpret_cast<const void*>(kern), dev);
+  if (!li.smem_set) {
+    const int rc = set_max_smem(reinterpret_cast<const void*>(kern), kHtSmem);
+    if (rc != MXW_OK) return rc;
+    li.per_sm = 2;
+    li.smem_set = true;
+  }
+  QuantParams P = P0;
+  P.n_row_tiles = (P.rows + kHtRows - 1) / kHtRows;
+  const int64_t n_tiles = ((P.nb + kHtCols - 1) / kHtCols) * P.n_row_tiles;
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(n_tiles, static_cast<int64_t>(num_sms()) * li.per_sm));
+  kern<<<static_cast<unsigned>(ctas), kHtThreads, kHtSmem, stream>>>(map, P);
+  const int rc = check_launch();
+  if (rc != MXW_OK) return rc;
+  QuantParams F = P0;
+  const int64_t chunks = (F.rows * F.nb + kFixupChunk - 1) / kFixupChunk;
+  const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()) * 2);
+  quantize_fixup_hess_kernel<DT, QM><<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, stream>>>(F);
+  return check_launch();
+}
+
 template <int DT, int OBJ, int QM>
 static int launch_plain(const void* w, int64_t ld, const QuantParams& P, cudaStream_t stream) {
   const int64_t total = P.rows * P.nb;
@@ -1304,6 +1945,12 @@ static int launch_any(const void* w, int64_t ld, const QuantParams& P, cudaStrea
 
 template <int DT, int OBJ>
 static int dispatch_q(int qm, const void* w, int64_t ld, const QuantParams& P, cudaStream_t s) {
+  if constexpr (OBJ == kObjHess && DT == MXW_BF16) {
+    const bool tma_ok = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && ((ld * 2) % 16 == 0) &&
+                        P.rows < (int64_t(1) << 31) && P.cols < (int64_t(1) << 31);
+    if (tma_ok && qm == kQTop2) return launch_hess_tc<DT, kQTop2>(w, ld, P, s);
+    if (tma_ok && qm == kQAmax) return launch_hess_tc<DT, kQAmax>(w, ld, P, s);
+  }
   if (qm == kQAmax) return launch_any<DT, OBJ, kQAmax>(w, ld, P, s);
   if (qm == kQTop2) return launch_any<DT, OBJ, kQTop2>(w, ld, P, s);
   return launch_any<DT, OBJ, kQGeneral>(w, ld, P, s);

@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(kStatThreads, GRAM ? 2 : 3)
   constexpr int RB = 32 * StatElem<DT>::kBytes;  // bytes per tile row
   // Unswizzled TMA tiles need 128-byte aligned destinations.
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint8_t* smem = align_smem<128>(smem_raw);
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStatStages * kStatTileBytes);
   uint64_t* empty = full + kStatStages;

@@ -17,10 +17,17 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // A pointer into dynamic shared memory rounded up to ALIGN bytes.  It stays
 // derived from the __shared__ array by pointer arithmetic (no round trip
 // through an integer), so the compiler keeps treating it as shared memory and
-// emits shared loads and stores through it rather than generic ones.
+// emits shared loads and stores through it rather than generic ones.  The
+// array's shared-window offset is read through inline PTX, which the
+// optimiser cannot see through: the dynamic array starts after any static
+// __shared__ variables, so it need not have the alignment its declaration
+// names, and a padding computed from the declared alignment would fold to 0.
 template <uint32_t ALIGN>
 __device__ __forceinline__ uint8_t* align_smem(uint8_t* smem_raw) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  uint32_t a;
+  asm volatile("{\n\t.reg .u64 t;\n\tcvta.to.shared.u64 t, %1;\n\tcvt.u32.u64 %0, t;\n\t}"
+               : "=r"(a)
+               : "l"(smem_raw));
   return smem_raw + (((a + ALIGN - 1) & ~(ALIGN - 1)) - a);
 }
 

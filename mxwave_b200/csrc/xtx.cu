@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "runtime.h"
+#include "tcgen05.cuh"
 #include "tma.cuh"
 
 namespace cg = cooperative_groups;
@@ -61,91 +62,6 @@ struct XtxParams {
   float* packed;  // non-null: add each tile's totals to its slot here instead of into gram
   uint32_t* flags;
 };
-
-// ---------------------------------------------------------- tcgen05 helpers
-
-__device__ __forceinline__ uint64_t make_smem_desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3fff);
-  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3fff) << 16;
-  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3fff) << 32;
-  d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
-  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor, kind::f16: bf16 A/B, fp32 D, both MN-major.
-__host__ __device__ constexpr uint32_t make_idesc_bf16_f32_mn(int m, int n) {
-  return (1u << 4)                                   // D format: f32
-         | (1u << 7)                                 // A format: bf16
-         | (1u << 10)                                // B format: bf16
-         | (1u << 15)                                // A major: MN
-         | (1u << 16)                                // B major: MN
-         | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
-         | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
-}
-
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void mma_bf16_f32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-// 32 lanes x 16 consecutive fp32 columns -> 16 registers per thread.
-__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int k = 0; k < 16; ++k) v[k] = __uint_as_float(r[k]);
-}
-
-// 32 lanes x 32 consecutive fp32 columns -> 32 registers per thread.
-__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
-}
 
 // ------------------------------------------------------------------- kernel
 
@@ -367,11 +283,13 @@ __global__ void __launch_bounds__(kXtxThreads, 1)
   if (threadIdx.x == 0 && *fail && P.flags) atomicOr(P.flags, MXW_FLAG_TIMEOUT);
 }
 
-// Adds packed tile totals (the layout xtx_kernel writes with P.packed) into G.
+// Adds packed tile totals (the layout xtx_kernel writes with P.packed) into G:
+// tiles first_tile + blockIdx.x, read from packed + blockIdx.x * tile.
 __global__ void __launch_bounds__(256) xtx_unpack_kernel(const float* __restrict__ packed, int64_t cols,
-                                                         int64_t n_col_tiles, float* gram, int64_t ldg) {
+                                                         int64_t n_col_tiles, float* gram, int64_t ldg,
+                                                         int64_t first_tile) {
   int64_t i0, j0;
-  xtx_tile_origin(blockIdx.x, n_col_tiles, i0, j0);
+  xtx_tile_origin(first_tile + blockIdx.x, n_col_tiles, i0, j0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quarter = warp & 3, half = warp >> 2;
   const float4* src = reinterpret_cast<const float4*>(packed + static_cast<int64_t>(blockIdx.x) * kXtxTileFloats +
@@ -714,6 +632,25 @@ extern "C" int mxw_xtx_unpack(const float* packed, int64_t cols, float* gram, in
   if (!packed || !gram) return MXW_EINVAL;
   if (reinterpret_cast<uintptr_t>(packed) % 16 != 0 || reinterpret_cast<uintptr_t>(gram) % 16 != 0) return MXW_EINVAL;
   xtx_unpack_kernel<<<static_cast<unsigned>(xtx_tiles(cols)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      packed, cols, (cols + kXtxBN - 1) / kXtxBN, gram, ldg);
+      packed, cols, (cols + kXtxBN - 1) / kXtxBN, gram, ldg, 0);
+  return check_launch();
+}
+
+extern "C" int64_t mxw_xtx_packed_tiles(int64_t cols) {
+  if (cols <= 0 || cols % 128 != 0 || cols >= (int64_t(1) << 31)) return 0;
+  return xtx_tiles(cols);
+}
+
+extern "C" int mxw_xtx_unpack_tiles(const float* packed, int64_t first_tile, int64_t n_tiles, int64_t cols,
+                                    float* gram, int64_t ldg, void* stream) {
+  if (cols <= 0 || cols % 128 != 0 || cols >= (int64_t(1) << 31) || ldg < cols || ldg % 4 != 0) return MXW_EINVAL;
+  if (first_tile < 0 || n_tiles < 0) return MXW_EINVAL;
+  const int64_t total = xtx_tiles(cols);
+  n_tiles = std::min<int64_t>(n_tiles, std::max<int64_t>(0, total - first_tile));  // padding tiles past the end
+  if (n_tiles == 0) return MXW_OK;
+  if (!packed || !gram) return MXW_EINVAL;
+  if (reinterpret_cast<uintptr_t>(packed) % 16 != 0 || reinterpret_cast<uintptr_t>(gram) % 16 != 0) return MXW_EINVAL;
+  xtx_unpack_kernel<<<static_cast<unsigned>(n_tiles), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      packed, cols, (cols + kXtxBN - 1) / kXtxBN, gram, ldg, first_tile);
   return check_launch();
 }

@@ -348,3 +348,35 @@ def test_rare_block_pass_runs_only_when_flagged(cuda_device) -> None:
         assert bool(int(flags.item()) & _lib.MXW_FLAG_RARE) == expect_rare
         po, so = oracle.quantize_mxfp4(arr)
         assert_same_bytes(arr, p.cpu().numpy(), s.cpu().numpy(), po, so)
+
+
+@pytest.mark.parametrize("kind", ["psd_few_tokens", "indefinite", "negative_diagonal", "pct100"])
+@pytest.mark.parametrize("depth", [0, 1, 4, 8])
+def test_block_hessian_screening_matches_oracle(kind, depth, cuda_device) -> None:
+    """The block-Hessian objective's tensor-core screening (bf16 weights):
+    Hessians from few tokens (many close calls, exact ties included through
+    dense outliers), indefinite and negative-diagonal matrices (the bound
+    without the Cauchy-Schwarz property), and the amax anchor.  Blocks the
+    screening cannot decide are re-quantized exactly; bytes must match the
+    oracle everywhere."""
+    rows, cols = 300, 2048 + 96  # a ragged last 128-row tile and an odd number of block columns
+    seed = 4000 + 17 * depth + len(kind)
+    w = syn.det_dense_weight(rows, cols, seed, outlier_fraction=0.05)
+    rng = np.random.default_rng(seed)
+    if kind in ("psd_few_tokens", "pct100"):
+        x = syn.bf16_bits_to_f32(syn.det_activations(8, cols, seed + 1)).astype(np.float64)
+        h = oracle.finalize_block_hessian(oracle.block_gram(x), 8, 1e-6, "absolute").astype(np.float32)
+    else:
+        a = rng.standard_normal((cols // 32, 32, 32)).astype(np.float32)
+        h = ((a + a.transpose(0, 2, 1)) * 0.5).astype(np.float32)
+        if kind == "indefinite":
+            h += np.eye(32, dtype=np.float32)[None] * 2.0  # symmetric, some negative eigenvalues
+        else:
+            h[:, np.arange(32), np.arange(32)] = -np.abs(h[:, np.arange(32), np.arange(32)])
+    kw: dict = {"mse_clip_depth": depth, "hessian": torch.from_numpy(h).to(cuda_device)}
+    okw: dict = {"mse_clip_depth": depth, "hessian": h}
+    if kind == "pct100":
+        kw["scale_percentile"] = okw["scale_percentile"] = 100.0
+    p, s = _gpu(_to_device(w, cuda_device), cuda_device, **kw)
+    po, so = oracle.quantize_mxfp4(w, **okw)
+    assert_same_bytes(w, p, s, po, so)
