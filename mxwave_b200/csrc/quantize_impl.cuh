@@ -792,8 +792,10 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
       second = __half2float(__ushort_as_half(static_cast<unsigned short>(top2)));
     }
   }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(release);
+  // Release the stage only once every lane's loads have returned: the arrive
+  // waits on a warp reduction of the statistics computed from them.
+  const uint32_t loaded = __reduce_or_sync(0xffffffffu, f32_bits(amax));  // sign clear: never all ones
+  if (lane == 0 && loaded != 0xffffffffu) mbar_arrive(release);
   unsigned long long unused_nt2[16];
   const float anchor = fmaxf(block_anchor<QM>(amax, second, unused_nt2, P), 1e-6f);
   const bool near_zero = amax < 1e-6f;
@@ -1067,8 +1069,8 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       } else {
         BlockData<DT> B;
         read_block_smem<DT, QM>(stages + s * kStageBytes, warp, lane, B);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        const uint32_t loaded = __reduce_or_sync(0xffffffffu, f32_bits(B.amax));  // as in quantize_block_fast
+        if (lane == 0 && loaded != 0xffffffffu) mbar_arrive(&empty[s]);
         if (active) {
           any_nonfinite |= B.nonfinite;
           sc = quantize_one_block<DT, OBJ, QM, true, true, OBJ != kObjHess>(B, P, g2, Hw, pk, Gw);
@@ -1244,7 +1246,7 @@ constexpr int kHtOffD = kHtStages * kHtStageBytes;
 constexpr int kHtOffH = kHtOffD + kHtRound * kHtCols * kHtDBytes;
 constexpr int kHtOffB = kHtOffH + kHtCols * 2 * kHtHBytes;
 constexpr int kHtOffBar = kHtOffB + kHtCols * 68 * 4;
-constexpr size_t kHtSmem = 1024 + kHtOffBar + (2 * kHtStages + 2) * 8 + 16;
+constexpr size_t kHtSmem = 1024 + kHtOffBar + (2 * kHtStages + 3) * 8 + 16;
 
 // Byte offset of row r's 16-byte chunk kc (elements 8kc .. 8kc+7) in a K-major
 // no-swizzle operand of K = 32: 8-row x 16-byte core matrices, 128 bytes
@@ -1302,7 +1304,8 @@ __global__ void __launch_bounds__(kHtThreads, 2)
   uint64_t* empty = full + kHtStages;
   uint64_t* d_ready = empty + kHtStages;
   uint64_t* mma_done = d_ready + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* strip_bar = mma_done + 1;  // the consumer warps' barrier around a block-column change
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(strip_bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_strips = (P.nb + kHtCols - 1) / kHtCols;
@@ -1319,6 +1322,7 @@ __global__ void __launch_bounds__(kHtThreads, 2)
     }
     mbar_init(d_ready, kHtConsumerWarps);
     mbar_init(mma_done, 1);
+    mbar_init(strip_bar, kHtConsumerWarps);
     fence_mbar_init();
   }
   if (warp == kHtMmaWarp) tmem_alloc(tmem_slot, kHtTmemCols);
@@ -1392,6 +1396,16 @@ __global__ void __launch_bounds__(kHtThreads, 2)
     int64_t cur_strip = -1;
     int64_t round = 0;
     int64_t i = 0;
+    uint32_t strip_phase = 0;
+    // All eight consumer warps meet here; bounded, so a warp that gave up on a
+    // wait cannot leave the others blocked.
+    auto strip_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(strip_bar);
+      const bool met = __all_sync(0xffffffffu, mbar_wait(strip_bar, strip_phase));
+      strip_phase ^= 1u;
+      return met;
+    };
     bool any_nonfinite = false, any_rare = false;
     TileCursor cur(t_begin, P.n_row_tiles);
     for (int64_t t = t_begin; t < t_end; ++t, ++i, cur.advance(P.n_row_tiles)) {
@@ -1416,11 +1430,32 @@ __global__ void __launch_bounds__(kHtThreads, 2)
           words[4 * j + 3] = v.w;
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      // Block statistics (they consume every loaded word) before the stage is
+      // released, and the release waits on a warp reduction of them: an
+      // mbarrier arrive issued right after the shared-memory loads could
+      // complete before their data returns, and the next TMA tile would then
+      // overwrite words still in flight.
+      uint32_t m1 = 0, m2 = 0;
+      unsigned long long t2[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t a = words[k] & 0x7fff7fffu;
+        if constexpr (QM == kQTop2) m2 = __vmaxu2(m2, __vminu2(m1, a));
+        m1 = __vmaxu2(m1, a);
+        t2[k] = word_pair<DT>(words[k]);
+      }
+      const uint32_t loaded = __reduce_or_sync(0xffffffffu, m1);  // <= 0x7fff7fff
+      if (lane == 0 && loaded != 0xffffffffu) mbar_arrive(&empty[s]);
       if (cur.strip != cur_strip) {
         // New block columns: both bf16 halves of H (as the MMA's K-major B
-        // operand: row n = d holds H[s][d] over s) and the bound data.
+        // operand: row n = d holds H[s][d] over s) and the bound data.  The
+        // barrier first: a warp still in the previous tile's epilogue reads
+        // the old bound data (the previous tile's MMAs, which read the old
+        // halves, have completed: every warp waited for them).
+        if (!strip_sync()) {
+          ok = false;
+          break;
+        }
         cur_strip = cur.strip;
         const int idx = r_tile;  // 128 threads per column: row d = idx / 4, chunk kc = idx % 4
         const int d = idx >> 2, kc = idx & 3;
@@ -1448,7 +1483,10 @@ __global__ void __launch_bounds__(kHtThreads, 2)
         rowsum = __fadd_ru(rowsum, __shfl_xor_sync(0xffffffffu, rowsum, 2));
         if (kc == 0) cb[32 + d] = rowsum;
         if (kc == (d >> 3)) cb[d] = hv[d & 7] >= 0.0f ? __fsqrt_ru(hv[d & 7]) : -1.0f;
-        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (!strip_sync()) {
+          ok = false;
+          break;
+        }
         // |H_sd| <= sqrt(H_ss) sqrt(H_dd) for every pair (true for a PSD H) lets
         // the tighter bound apply; checked on the rounded-up square roots.
 #pragma unroll
@@ -1459,22 +1497,16 @@ __global__ void __launch_bounds__(kHtThreads, 2)
         cs = __all_sync(0xffffffffu, cs);
         if (lane == 0) reinterpret_cast<int*>(cb)[64 + quarter] = cs ? 1 : 0;
         fence_proxy_async_smem();
-        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (!strip_sync()) {
+          ok = false;
+          break;
+        }
       }
       const float* cb = bnd + col * 68;
       const int* csf = reinterpret_cast<const int*>(cb + 64);
       const bool use_cs = csf[0] && csf[1] && csf[2] && csf[3];
 
-      // Block statistics, anchor and candidate exponents (as quantize_block_fast).
-      uint32_t m1 = 0, m2 = 0;
-      unsigned long long t2[16];
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const uint32_t a = words[k] & 0x7fff7fffu;
-        if constexpr (QM == kQTop2) m2 = __vmaxu2(m2, __vminu2(m1, a));
-        m1 = __vmaxu2(m1, a);
-        t2[k] = word_pair<DT>(words[k]);
-      }
+      // Anchor and candidate exponents (as quantize_block_fast).
       float amax, second;
       bool nonfinite;
       {

@@ -14,10 +14,12 @@ result.  The implementation is this package's own:
   routes are grouped by expert with a stable sort, and each expert's squared,
   routing-weighted activations are summed in route order in fp64 and added
   once -- deterministic, unlike an atomic ``index_add_``;
-* ``finalize`` computes every expert's gamma at once on the device
-  (sqrt(squares / mass), normalised by its maximum, in fp32 with IEEE
-  division and square root, as the reference's per-expert CPU loop rounds
-  them) and brings only the finished gammas, masses and counts to the host.
+* ``finalize`` divides every expert's squares by its routing mass at once on
+  the device (IEEE division, which is how the reference's CPU division
+  rounds) and brings the quotients, masses and counts to the host in one
+  transfer; the square root and the normalisation by the maximum then use
+  torch's CPU kernels per expert row, as the reference does, because
+  torch's vectorised CPU square root is not correctly rounded.
 """
 
 from __future__ import annotations
@@ -57,14 +59,12 @@ def _accumulate(squares: torch.Tensor, mass: torch.Tensor | None, inputs: torch.
     _lib.check(status, "mxw_accumulate_routed_squares")
 
 
-def _device_gammas(squares: torch.Tensor, mass: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Per expert: sqrt(squares / mass) / its maximum, and whether the expert is calibrated."""
+def _device_quotients(squares: torch.Tensor, mass: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per expert: squares / mass (IEEE division, as the reference's CPU division rounds) and
+    whether the expert is calibrated (positive mass and some positive square)."""
     usable = (mass > 0) & (squares > 0).any(dim=1)
     safe_mass = torch.where(mass > 0, mass, torch.ones_like(mass))
-    root = torch.sqrt(squares / safe_mass[:, None])
-    peak = root.amax(dim=1, keepdim=True)
-    gamma = root / torch.where(peak > 0, peak, torch.ones_like(peak))
-    return gamma, usable
+    return squares / safe_mass[:, None], usable
 
 
 @dataclass
@@ -135,10 +135,10 @@ class RoutedLayerMoments:
         finite = torch.isfinite(self.input_squares).all() & torch.isfinite(self.down_squares).all()
         if not bool(finite):
             raise ValueError("Captured activation moments contain NaN or infinity")
-        gate_gamma, gate_ok = _device_gammas(self.input_squares, self.route_mass)
-        down_gamma, down_ok = _device_gammas(self.down_squares, self.route_mass)
+        gate_q, gate_ok = _device_quotients(self.input_squares, self.route_mass)
+        down_q, down_ok = _device_quotients(self.down_squares, self.route_mass)
         # One host transfer of everything the result needs.
-        gate_gamma, down_gamma = gate_gamma.cpu(), down_gamma.cpu()
+        gate_q, down_q = gate_q.cpu(), down_q.cpu()
         flags = torch.stack([gate_ok, down_ok]).cpu().tolist()
         masses = self.route_mass.cpu().tolist()
         counts = self.observations.cpu().tolist()
@@ -151,7 +151,12 @@ class RoutedLayerMoments:
                 if not flags[1 if down else 0][expert]:
                     retained.append(name)
                     continue
-                statistics[name] = (down_gamma if down else gate_gamma)[expert].clone()
+                # The square root and the normalisation run on the host with torch's CPU
+                # kernels, one expert row at a time as the reference applies them: torch's
+                # vectorised CPU sqrt is not correctly rounded, so the device's IEEE sqrt would
+                # differ from the reference's gammas in the last bit.
+                root = torch.sqrt((down_q if down else gate_q)[expert])
+                statistics[name] = (root / root.amax()).float().contiguous()
         return statistics, {
             "layer": layer,
             "routed_observations": counts,

@@ -205,6 +205,7 @@ def test_engine_stream_chunks_match_reference_loop(tmp_path, cuda_device) -> Non
     shard = shard_mod.ShardFile(path=path, weight_map={})
     infos = shard_mod.shard_tensor_info(shard)
     gamma = torch.rand(1024) + 0.25
+    errors = {}
     for name, kw in (("a.weight", {}), ("a.weight", {"gamma": gamma}), ("b.weight", {}), ("c.weight", {})):
         base = dict(model_dir=tmp_path, output_dir=tmp_path / "o", policy="all-linear", verbose=False,
                     tensor_row_chunk_size=96, tensor_chunk_max_elements=1 << 20)
@@ -223,7 +224,9 @@ def test_engine_stream_chunks_match_reference_loop(tmp_path, cuda_device) -> Non
         for (_, _, gp, gs, dev), (_, _, wp, ws, _) in zip(got[0], want[0]):
             assert dev == "cpu"  # host chunks: the writer's .cpu() is a no-op
             assert torch.equal(gp, wp) and torch.equal(gs, ws)
-    assert want[1] is not None and "rows [576, 672)" in want[1]
+        errors[name] = want[1]
+    assert errors["b.weight"] is not None and "rows [576, 672)" in errors["b.weight"]
+    assert errors["a.weight"] is None and errors["c.weight"] is None
 
 
 def test_engine_stream_defers_to_a_patched_quantizer(tmp_path, cuda_device) -> None:

@@ -155,3 +155,26 @@ def test_moment_and_gram_oracles_match_reference_collector() -> None:
     h = oracle.finalize_block_hessian(oracle.block_gram(xf), 512, 1e-6, "absolute")
     scale = np.sqrt(np.einsum("bii->bi", h)[:, :, None] * np.einsum("bii->bi", h)[:, None, :])
     assert np.max(np.abs(st["block-hessian"]["p.weight"].numpy() - h) / scale) < 1e-5
+
+
+@pytest.mark.parametrize("short,objective", [("self_attn.k_proj", "hess"), ("self_attn.k_proj", "rms"),
+                                             ("self_attn.o_proj", "hess"), ("self_attn.v_proj", "hess")])
+def test_oracle_matches_decoder_layer_reference_sha(short, objective) -> None:
+    """The oracle reproduces the reference's hashes on linears of the decoder
+    layer quantized with the statistics of the reference's own sequential
+    calibration (tests/golden/layer_golden.py)."""
+    from tests.golden.fixtures import load_layer_stats
+    from tests.golden.layer_specs import LAYER_INPUT_GROUP, LAYER_LINEARS, layer_seed
+
+    stats = load_layer_stats()
+    cfg = load_configs()
+    key = f"layer_{short}_{objective}_d1"
+    if key not in cfg or not stats:
+        pytest.skip("layer fixtures not generated")
+    rows, cols = LAYER_LINEARS[short]
+    bits = syn.det_dense_weight(rows, cols, seed=layer_seed(short), outlier_fraction=0.0)
+    group = LAYER_INPUT_GROUP[short]
+    kw = {"hessian": stats[f"layer_hess_{group}"]} if objective == "hess" else {"gamma": stats[f"layer_rms_{group}"]}
+    p, s = oracle.quantize_mxfp4(bits, mse_clip_depth=1, **kw)
+    assert _sha(p) == cfg[key]["packed_sha256"]
+    assert _sha(s) == cfg[key]["scales_sha256"]
