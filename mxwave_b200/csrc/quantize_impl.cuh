@@ -1156,9 +1156,11 @@ __device__ __forceinline__ void fixup_block(const QuantParams& P, int64_t idx) {
 }
 
 template <int DT, int OBJ, int QM>
-__global__ void __launch_bounds__(256) quantize_fixup_kernel(const QuantParams P) {
-  // With a flag word, the main pass reported whether it marked any block.
-  if (P.flags && (*reinterpret_cast<volatile const uint32_t*>(P.flags) & MXW_FLAG_RARE) == 0) return;
+__global__ void __launch_bounds__(256) quantize_fixup_kernel(const QuantParams P, const uint32_t gate) {
+  // With a flag word, the earlier passes reported whether any block can be
+  // marked: MXW_FLAG_RARE after the main pass, MXW_FLAG_NONFINITE after the
+  // block-Hessian exact pass (which leaves only non-finite blocks marked).
+  if (P.flags && (*reinterpret_cast<volatile const uint32_t*>(P.flags) & gate) == 0) return;
   const int64_t total = P.rows * P.nb;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -1202,15 +1204,18 @@ __global__ void __launch_bounds__(256) quantize_fixup_kernel(const QuantParams P
 // that on CUDA cores costs 1,024 FMA per block and candidate, reading H from
 // shared memory for each.  Here the tensor cores screen instead:
 //
-//   * D is exact in bf16 (at most 8 significant bits: t has 8 and q*2^e - t
-//     is a multiple of t's last place no larger than |t|), and H = Hh + Hl
-//     in two bf16 halves to 2^-16 relative;
+//   * the screening works on D / 2^e = q(x) - x (x = t / 2^e): the form
+//     scales exactly by 2^(2e).  It is exact in bf16 when |x| < 512 (at most
+//     8 significant bits: t has 8 and q - x is a multiple of x's last place
+//     no larger than |x|), and H = Hh + Hl in two bf16 halves to 2^-16
+//     relative;
 //   * per tile of 128 rows x 2 block columns, each thread writes its block's
-//     D for up to 4 candidates into shared memory (K-major, no swizzle), and
-//     one thread issues tcgen05.mma (M = 128 rows, N = 32, K = 32, both H
-//     halves) into TMEM: W = D * H for every row at once;
+//     D / 2^e for up to 4 candidates into shared memory (K-major, no
+//     swizzle), and one thread issues tcgen05.mma (M = 128 rows, N = 32,
+//     K = 32, both H halves) into TMEM: W = D * H for every row at once;
 //   * each thread reads its row of W back (tcgen05.ld) and forms
-//     E' = sum_d W_d D_d, with a bound |E' - E_reference| <= 4e-5 * A where
+//     E' = sum_d W_d D_d in packed fp32 pairs, with a bound
+//     |E' - E_reference| <= 4e-5 * A where
 //     A >= sum_{s,d} |D_s| |H_sd| |D_d| (2^-16 from the split, 2^-17 from the
 //     tensor core's fp32 accumulation, about 46 fp32 roundings on each side);
 //     A is (sum_s |D_s| sqrt(H_ss))^2 when every |H_sd| <= sqrt(H_ss H_dd)
@@ -1218,7 +1223,8 @@ __global__ void __launch_bounds__(256) quantize_fixup_kernel(const QuantParams P
 //   * the candidate with the least E' (earliest on ties) is the reference's
 //     choice when every other candidate's E' exceeds it by more than both
 //     bounds; otherwise the block gets the rare marker and
-//     quantize_fixup_kernel evaluates it exactly.
+//     quantize_fixup_hess_kernel evaluates it exactly, one warp per block
+//     (blocks with non-finite elements: quantize_fixup_kernel, one thread).
 //
 // Candidates follow the reference's order (core.py:201-209): f - depth ..
 // f + 1, then the no-clipping exponent when it is f + 2.  Blocks outside
@@ -1273,29 +1279,82 @@ __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
   return r;
 }
 
-// D = q(t / 2^e) * 2^e - t for the block's 16 element pairs, as bf16 pairs (exact).
-__device__ __forceinline__ void ht_candidate_d(const unsigned long long (&t2)[16], int e, float zero,
-                                               uint32_t (&d)[16]) {
-  const float inv = exp2i(-e), sc = exp2i(e);
-  const unsigned long long I2 = pack2(inv, inv), S2 = pack2(sc, sc), Z2 = pack2(zero, zero);
+// D / 2^e = q(x) - x with x = t / 2^e, for the block's 16 element pairs, as
+// bf16 pairs (exact whenever |x| < 512).  The quadratic form scales exactly
+// with 2^(2e), so the screening works on D / 2^e and rescales its result.  Per
+// element: x = t * 2^-e from the bf16 word half by one mixed-precision fma
+// (exact), E2M1 round trip by hardware RNE, and q - x by one mixed-precision
+// subtraction on q's f16 value (exact in fp32).  The sign of a zero is
+// irrelevant here: D enters only the quadratic form and its bound.
+__device__ __forceinline__ void ht_candidate_d(const uint32_t (&words)[16], int e, uint32_t (&d)[16]) {
+  const uint16_t inv = static_cast<uint16_t>(static_cast<uint32_t>(127 - e) << 7);  // bf16 2^-e (|e| < 100 here)
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    unsigned long long x[4];
-    uint32_t h[4];
+  for (int j = 0; j < 16; ++j) {
+    float x0, x1, d0, d1;
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, lo, %3, %4;\n\tfma.rn.f32.bf16 %1, hi, %3, %4;\n\t}"
+        : "=f"(x0), "=f"(x1) : "r"(words[j]), "h"(inv), "f"(0.0f));
+    asm("{\n\t.reg .b8 c;\n\t.reg .b32 h;\n\t.reg .b16 q0, q1;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 c, %3, %2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 h, c;\n\t"
+        "mov.b32 {q0, q1}, h;\n\t"
+        "sub.rn.f32.f16 %0, q0, %2;\n\t"
+        "sub.rn.f32.f16 %1, q1, %3;\n\t}"
+        : "=f"(d0), "=f"(d1) : "f"(x0), "f"(x1));
+    d[j] = bf16x2_rn(d0, d1);
+  }
+}
+
+__device__ __forceinline__ unsigned long long fma2_rp(unsigned long long a, unsigned long long b,
+                                                      unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rp.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// One candidate's row of the screening, in units of 2^(2e): E' = sum_d W_d D_d
+// (W = D H from TMEM, D from its bf16 words in the core layout) and the bound
+// A >= sum_{s,d} |D_s| |H_sd| |D_d| on the terms the reference rounds:
+// (sum_s |D_s| sqrt(H_ss))^2 when the block column passed the Cauchy-Schwarz
+// check (CS), else max|D| * sum_s |D_s| rowsum_s.  Packed pairs: two RN chains
+// for E' and two round-up chains for the linear sum.
+template <bool CS>
+__device__ __forceinline__ void ht_epilogue(const float (&w)[32], uint32_t src, int r_tile, const float* cb,
+                                            float& e_out, float& a_out) {
+  unsigned long long ea = 0ull, eb = 0ull, aa = 0ull, ab = 0ull;
+  uint32_t dm = 0u;
+  const float4* coef = reinterpret_cast<const float4*>(cb + (CS ? 0 : 32));
+  // Element pair (s, s + 1) from bf16 word `v`, coefficients (c0, c1).
+  auto pair = [&](uint32_t v, int sidx, float c0, float c1, unsigned long long& e, unsigned long long& a) {
+    const uint32_t lo = v << 16, hi = v & 0xffff0000u;
+    e = fma2(pack2(w[sidx], w[sidx + 1]), pack2(bits_f32(lo), bits_f32(hi)), e);
+    a = fma2_rp(pack2(bits_f32(lo & 0x7fffffffu), bits_f32(hi & 0x7fffffffu)), pack2(c0, c1), a);
+    if constexpr (!CS) dm = __vmaxu2(dm, v & 0x7fff7fffu);
+  };
 #pragma unroll
-    for (int k = 0; k < 4; ++k) x[k] = fma2(t2[4 * q + k], I2, Z2);
-    e2m1_quad(x, h);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const f2 v = unpack2(fma2(f16x2_to_f32x2(h[k]), S2, t2[4 * q + k] ^ 0x8000000080000000ull));
-      d[4 * q + k] = bf16x2_rn(v.x, v.y);
-    }
+  for (int kc = 0; kc < 4; ++kc) {
+    const uint4 v = lds128(src + ht_core_offset(r_tile, kc));
+    const float4 c0 = coef[2 * kc], c1 = coef[2 * kc + 1];
+    pair(v.x, 8 * kc, c0.x, c0.y, ea, aa);
+    pair(v.y, 8 * kc + 2, c0.z, c0.w, eb, ab);
+    pair(v.z, 8 * kc + 4, c1.x, c1.y, ea, aa);
+    pair(v.w, 8 * kc + 6, c1.z, c1.w, eb, ab);
+  }
+  const f2 e0 = unpack2(ea), e1 = unpack2(eb), a0 = unpack2(aa), a1 = unpack2(ab);
+  e_out = __fadd_rn(__fadd_rn(e0.x, e0.y), __fadd_rn(e1.x, e1.y));
+  const float a_lin = __fadd_ru(__fadd_ru(a0.x, a0.y), __fadd_ru(a1.x, a1.y));
+  if constexpr (CS) {
+    a_out = __fmul_ru(a_lin, a_lin);
+  } else {
+    const float d_max = bits_f32(max(dm & 0xffffu, dm >> 16) << 16);
+    a_out = __fmul_ru(a_lin, d_max);
   }
 }
 
 template <int DT, int QM>
 __global__ void __launch_bounds__(kHtThreads, 2)
     quantize_hess_tc_kernel(const __grid_constant__ CUtensorMap map, const QuantParams P) {
+  static_assert(DT == MXW_BF16, "the screening forms D from bf16 words");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = align_smem<1024>(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -1436,13 +1495,11 @@ __global__ void __launch_bounds__(kHtThreads, 2)
       // complete before their data returns, and the next TMA tile would then
       // overwrite words still in flight.
       uint32_t m1 = 0, m2 = 0;
-      unsigned long long t2[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
         const uint32_t a = words[k] & 0x7fff7fffu;
         if constexpr (QM == kQTop2) m2 = __vmaxu2(m2, __vminu2(m1, a));
         m1 = __vmaxu2(m1, a);
-        t2[k] = word_pair<DT>(words[k]);
       }
       const uint32_t loaded = __reduce_or_sync(0xffffffffu, m1);  // <= 0x7fff7fff
       if (lane == 0 && loaded != 0xffffffffu) mbar_arrive(&empty[s]);
@@ -1548,7 +1605,7 @@ __global__ void __launch_bounds__(kHtThreads, 2)
           if (c >= cmax) break;
           uint32_t dw[16];
           if (fast && c < ncand) {
-            ht_candidate_d(t2, c < P.depth + 2 ? f - P.depth + c : safe_e, P.zero, dw);
+            ht_candidate_d(words, c < P.depth + 2 ? f - P.depth + c : safe_e, dw);
           } else {
 #pragma unroll
             for (int k = 0; k < 16; ++k) dw[k] = 0u;
@@ -1575,34 +1632,23 @@ __global__ void __launch_bounds__(kHtThreads, 2)
           tmem_ld_32x32b_x32(tl + static_cast<uint32_t>((cl * kHtCols + col) * 32), w);
           if (!(fast && c < ncand)) continue;
           const uint32_t src = my_d + cl * kHtCols * kHtDBytes;
-          float e_acc = 0.0f, a_lin = 0.0f, d_max = 0.0f;
-          const float4* coef = reinterpret_cast<const float4*>(cb + (use_cs ? 0 : 32));
-          float e_acc2 = 0.0f;
-#pragma unroll
-          for (int kc = 0; kc < 4; ++kc) {
-            const uint4 v = lds128(src + ht_core_offset(r_tile, kc));
-            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-            const float4 ca = coef[2 * kc], cc = coef[2 * kc + 1];
-            const float cf[8] = {ca.x, ca.y, ca.z, ca.w, cc.x, cc.y, cc.z, cc.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int sidx = 8 * kc + 2 * k;
-              const float d0 = bits_f32(vv[k] << 16), d1 = bits_f32(vv[k] & 0xffff0000u);
-              e_acc = __fmaf_rn(w[sidx], d0, e_acc);
-              e_acc2 = __fmaf_rn(w[sidx + 1], d1, e_acc2);
-              a_lin = __fmaf_ru(fabsf(d0), cf[2 * k], a_lin);
-              a_lin = __fmaf_ru(fabsf(d1), cf[2 * k + 1], a_lin);
-              d_max = fmaxf(d_max, fmaxf(fabsf(d0), fabsf(d1)));
-            }
+          float e_sc, a_sc;
+          if (use_cs) {
+            ht_epilogue<true>(w, src, r_tile, cb, e_sc, a_sc);
+          } else {
+            ht_epilogue<false>(w, src, r_tile, cb, e_sc, a_sc);
           }
-          e_acc = __fadd_rn(e_acc, e_acc2);
-          const float a_bound = use_cs ? __fmul_ru(a_lin, a_lin) : __fmul_ru(a_lin, d_max);
-          // D is exact in bf16 unless a clipped element has |t| / 2^e >= 512
-          // (then |x| - 6 needs more than 8 bits); its rounding (2^-8 relative
-          // per element) enters the quadratic form twice.
+          // Back to the reference's units: E = E' * 2^(2e), exact for the
+          // exponents here (-40 < e < 20).  D is exact in bf16 unless a clipped
+          // element has |t| / 2^e >= 512 (then |x| - 6 needs more than 8 bits);
+          // its rounding (2^-8 relative per element) enters the form twice.
           const int ec = c < P.depth + 2 ? f - P.depth + c : safe_e;
-          const float tol = __fmul_ru(a_bound, amax_exp - ec >= 9 ? kHtTolInexact : kHtTol);
-          if (isnan(e_acc) || !(tol < __int_as_float(0x7f800000))) bad = true;
+          const float s2 = exp2i(2 * ec);
+          const float e_acc = __fmul_rn(e_sc, s2);
+          const float tol = __fmul_ru(__fmul_ru(a_sc, s2), amax_exp - ec >= 9 ? kHtTolInexact : kHtTol);
+          // A bound far down in the subnormal range no longer covers the
+          // absolute rounding of the reference's intermediates: exact pass.
+          if (isnan(e_acc) || !(tol < __int_as_float(0x7f800000)) || (a_sc > 0.0f && !(tol >= 0x1p-100f))) bad = true;
           if (e_acc < best) {
             runner = fminf(runner, __fsub_rd(best, best_tol));
             best = e_acc;
@@ -1623,7 +1669,7 @@ __global__ void __launch_bounds__(kHtThreads, 2)
         sc = static_cast<uint32_t>(floor_log2_div6(anchor) - P.depth + 127);  // all-zero codes (core.py:194-195)
       } else if (decided) {
         const int raw = best_c < P.depth + 2 ? f - P.depth + best_c : safe_e;
-        encode_pairs([&](int j) { return t2[j]; }, P, raw, pk);
+        encode_pairs([&](int j) { return word_pair<DT>(words[j]); }, P, raw, pk);
         sc = static_cast<uint32_t>(raw + 127);
       } else {
         sc = kRareBlock;
@@ -1705,16 +1751,9 @@ __device__ __forceinline__ void warp_fixup_hessian_block(const QuantParams& P, i
     }
   }
   const uint32_t a = f32_bits(t) & 0x7fffffffu;
-  if (__any_sync(0xffffffffu, a >= 0x7f800000u)) {
-    // Non-finite elements: the single-thread exact path replays the reference's NaN handling.
-    if (lane == 0) {
-      uint4 pk;
-      const uint32_t sc = quantize_block_slow<DT, kObjHess, QM>(P, row, blk, &pk);
-      *reinterpret_cast<uint4*>(P.packed + row * (P.cols / 2) + blk * 16) = pk;
-      P.scales[idx] = static_cast<uint8_t>(sc);
-    }
-    return;
-  }
+  // Non-finite elements: left marked for the single-thread exact pass, which
+  // replays the reference's NaN handling.
+  if (__any_sync(0xffffffffu, a >= 0x7f800000u)) return;
   // Top-2 magnitudes (ties: the second equals the first).
   const uint32_t m1 = __reduce_max_sync(0xffffffffu, a);
   const uint32_t n1 = __popc(__ballot_sync(0xffffffffu, a == m1));
@@ -1768,7 +1807,7 @@ __device__ __forceinline__ void warp_fixup_hessian_block(const QuantParams& P, i
 // re-quantizes each with a whole warp.  Each warp reads 512 scale bytes per
 // step (16 per lane); returns at once when the main pass marked nothing.
 template <int DT, int QM>
-__global__ void __launch_bounds__(256) quantize_fixup_hess_kernel(const QuantParams P) {
+__global__ void __launch_bounds__(256, 4) quantize_fixup_hess_kernel(const QuantParams P) {
   if (P.flags && (*reinterpret_cast<volatile const uint32_t*>(P.flags) & MXW_FLAG_RARE) == 0) return;
   const int lane = threadIdx.x & 31;
   const int64_t total = P.rows * P.nb;
@@ -1921,7 +1960,7 @@ static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStre
     if (rc != MXW_OK) return rc;
     const int64_t chunks = (P.rows * P.nb + kFixupChunk - 1) / kFixupChunk;
     const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()) * 2);
-    quantize_fixup_kernel<DT, OBJ, QM><<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, stream>>>(P);
+    quantize_fixup_kernel<DT, OBJ, QM><<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, stream>>>(P, MXW_FLAG_RARE);
     return check_launch();
   }
   return rc;
@@ -1953,9 +1992,18 @@ static int launch_hess_tc(const void* w, int64_t ld, const QuantParams& P0, cuda
   const int rc = check_launch();
   if (rc != MXW_OK) return rc;
   QuantParams F = P0;
-  const int64_t chunks = (F.rows * F.nb + kFixupChunk - 1) / kFixupChunk;
-  const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()) * 2);
+  // One warp per 512 scale bytes, up to four 8-warp CTAs per SM: the marked
+  // blocks spread over as many warps as the scan has steps.
+  const int64_t steps = (F.rows * F.nb + 511) / 512;
+  const int64_t blocks = std::min<int64_t>((steps + 7) / 8, static_cast<int64_t>(num_sms()) * 4);
   quantize_fixup_hess_kernel<DT, QM><<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, stream>>>(F);
+  const int rc2 = check_launch();
+  if (rc2 != MXW_OK) return rc2;
+  // Blocks with non-finite elements (returns at once when the main pass saw none).
+  const int64_t chunks = (F.rows * F.nb + kFixupChunk - 1) / kFixupChunk;
+  const int64_t nf_blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()) * 2);
+  quantize_fixup_kernel<DT, kObjHess, QM><<<static_cast<unsigned>(std::max<int64_t>(nf_blocks, 1)), 256, 0, stream>>>(
+      F, MXW_FLAG_NONFINITE);
   return check_launch();
 }
 
