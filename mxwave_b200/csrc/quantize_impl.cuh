@@ -1236,10 +1236,12 @@ constexpr int kHtRows = 128;                              // weight rows per til
 constexpr int kHtCols = 2;                                // block columns per tile
 constexpr int kHtStages = 2;
 constexpr int kHtStageBytes = kHtRows * 128;              // 128 rows x 64 two-byte elements
-constexpr int kHtRound = 4;                               // candidates per MMA round
+constexpr int kHtRound = 2;                               // candidates per MMA round
+constexpr int kHtBufs = 2;                                // rounds in flight (D and TMEM buffers)
 constexpr int kHtDBytes = kHtRows * 64;                   // bf16 D of one candidate and block column
 constexpr int kHtHBytes = 32 * 64;                        // one bf16 half of a 32x32 block Hessian
-constexpr uint32_t kHtTmemCols = kHtRound * kHtCols * 32;  // 256
+constexpr uint32_t kHtTmemCols = kHtBufs * kHtRound * kHtCols * 32;  // 256
+constexpr uint32_t kHtTmemBuf = kHtRound * kHtCols * 32;
 constexpr int kHtConsumerWarps = 8;
 constexpr int kHtProducerWarp = 8;
 constexpr int kHtMmaWarp = 9;
@@ -1249,10 +1251,11 @@ constexpr float kHtTolInexact = 4e-5f + 0.0079f;  // plus (2 * 2^-8 + 2^-16) x 1
 // Shared memory: stages | D [round][col] | H halves [col][hi, lo] | per-column
 // bound data (sqrt(H_ss) and sum_d |H_sd|, 32 each, then the CS flag) | barriers.
 constexpr int kHtOffD = kHtStages * kHtStageBytes;
-constexpr int kHtOffH = kHtOffD + kHtRound * kHtCols * kHtDBytes;
+constexpr int kHtDBuf = kHtRound * kHtCols * kHtDBytes;    // one round's D
+constexpr int kHtOffH = kHtOffD + kHtBufs * kHtDBuf;
 constexpr int kHtOffB = kHtOffH + kHtCols * 2 * kHtHBytes;
 constexpr int kHtOffBar = kHtOffB + kHtCols * 68 * 4;
-constexpr size_t kHtSmem = 1024 + kHtOffBar + (2 * kHtStages + 3) * 8 + 16;
+constexpr size_t kHtSmem = 1024 + kHtOffBar + (2 * kHtStages + 2 * kHtBufs + 1) * 8 + 16;
 
 // Byte offset of row r's 16-byte chunk kc (elements 8kc .. 8kc+7) in a K-major
 // no-swizzle operand of K = 32: 8-row x 16-byte core matrices, 128 bytes
@@ -1361,9 +1364,9 @@ __global__ void __launch_bounds__(kHtThreads, 2)
   float* bnd = reinterpret_cast<float*>(smem + kHtOffB);  // [col][68]: sqrt(H_ss) x32, row sums x32, flag
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kHtOffBar);
   uint64_t* empty = full + kHtStages;
-  uint64_t* d_ready = empty + kHtStages;
-  uint64_t* mma_done = d_ready + 1;
-  uint64_t* strip_bar = mma_done + 1;  // the consumer warps' barrier around a block-column change
+  uint64_t* d_ready = empty + kHtStages;    // [kHtBufs]: a round's D is in shared memory
+  uint64_t* mma_done = d_ready + kHtBufs;   // [kHtBufs]: a round's products are in TMEM
+  uint64_t* strip_bar = mma_done + kHtBufs;  // the consumer warps' barrier around a block-column change
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(strip_bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1379,8 +1382,10 @@ __global__ void __launch_bounds__(kHtThreads, 2)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kHtConsumerWarps);
     }
-    mbar_init(d_ready, kHtConsumerWarps);
-    mbar_init(mma_done, 1);
+    for (int b = 0; b < kHtBufs; ++b) {
+      mbar_init(&d_ready[b], kHtConsumerWarps);
+      mbar_init(&mma_done[b], 1);
+    }
     mbar_init(strip_bar, kHtConsumerWarps);
     fence_mbar_init();
   }
@@ -1412,19 +1417,24 @@ __global__ void __launch_bounds__(kHtThreads, 2)
   } else if (warp == kHtMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_bf16_f32_k(kHtRows, 32);
+      // Rounds in order, alternating between the two D / TMEM buffers; round g
+      // uses buffer g % 2, whose barriers complete once per use (parity g / 2).
       int64_t round = 0;
       for (int64_t t = t_begin; t < t_end && ok; ++t) {
         for (int r = 0; r < n_rounds; ++r, ++round) {
-          if (!mbar_wait(d_ready, static_cast<uint32_t>(round & 1))) {
+          const int buf = static_cast<int>(round & 1);
+          if (!mbar_wait(&d_ready[buf], static_cast<uint32_t>((round >> 1) & 1))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          for (int cl = 0; cl < kHtRound && r * kHtRound + cl < cmax; ++cl) {
+#pragma unroll
+          for (int cl = 0; cl < kHtRound; ++cl) {
+            if (r * kHtRound + cl >= cmax) break;
 #pragma unroll
             for (int col = 0; col < kHtCols; ++col) {
-              const uint32_t d_tmem = tmem + static_cast<uint32_t>((cl * kHtCols + col) * 32);
-              const uint32_t a = sbase + kHtOffD + (cl * kHtCols + col) * kHtDBytes;
+              const uint32_t d_tmem = tmem + buf * kHtTmemBuf + static_cast<uint32_t>((cl * kHtCols + col) * 32);
+              const uint32_t a = sbase + kHtOffD + buf * kHtDBuf + (cl * kHtCols + col) * kHtDBytes;
               const uint32_t b = sbase + kHtOffH + col * 2 * kHtHBytes;
 #pragma unroll
               for (int ks = 0; ks < 2; ++ks) {
@@ -1437,20 +1447,20 @@ __global__ void __launch_bounds__(kHtThreads, 2)
               }
             }
           }
-          mma_commit(mma_done);
+          mma_commit(&mma_done[buf]);
         }
       }
       if (!ok) {
         // Let consumers still waiting on a round see it finish; the timeout flag
         // makes the caller discard the output.
-        for (; round < (t_end - t_begin) * n_rounds; ++round) mma_commit(mma_done);
+        for (; round < (t_end - t_begin) * n_rounds; ++round) mma_commit(&mma_done[round & 1]);
       }
     }
   } else {
     // ------------------------------------------------- consumers: one block per thread
     const int quarter = warp & 3, col = warp >> 2;
     const int r_tile = quarter * 32 + lane;  // this thread's row of the tile (= TMEM lane)
-    const uint32_t my_d = sbase + kHtOffD + col * kHtDBytes;
+    const uint32_t my_d = sbase + kHtOffD + col * kHtDBytes;  // + buffer * kHtDBuf + candidate * kHtCols * kHtDBytes
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
     int64_t cur_strip = -1;
     int64_t round = 0;
@@ -1598,7 +1608,12 @@ __global__ void __launch_bounds__(kHtThreads, 2)
       // against the final best needs min over c != best of (E'_c - tol_c).
       float runner = __int_as_float(0x7f800000);  // min of E'_c - tol_c over c != best_c
       bool bad = false;
-      for (int r = 0; r < n_rounds; ++r, ++round) {
+      // Rounds of up to kHtRound candidates, two in flight: round r + 1's D is
+      // formed while round r's products are computed, and a buffer is refilled
+      // (round r + 2) only after round r's epilogue has read it.
+      const int64_t g0 = round;
+      auto form = [&](int r) {
+        const int buf = static_cast<int>((g0 + r) & 1);
 #pragma unroll
         for (int cl = 0; cl < kHtRound; ++cl) {
           const int c = r * kHtRound + cl;
@@ -1610,7 +1625,7 @@ __global__ void __launch_bounds__(kHtThreads, 2)
 #pragma unroll
             for (int k = 0; k < 16; ++k) dw[k] = 0u;
           }
-          const uint32_t dst = my_d + cl * kHtCols * kHtDBytes;
+          const uint32_t dst = my_d + buf * kHtDBuf + cl * kHtCols * kHtDBytes;
 #pragma unroll
           for (int kc = 0; kc < 4; ++kc)
             sts128(dst + ht_core_offset(r_tile, kc), make_uint4(dw[4 * kc], dw[4 * kc + 1], dw[4 * kc + 2], dw[4 * kc + 3]));
@@ -1618,20 +1633,21 @@ __global__ void __launch_bounds__(kHtThreads, 2)
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(d_ready);
-        if (!__all_sync(0xffffffffu, mbar_wait(mma_done, static_cast<uint32_t>(round & 1)))) {
-          ok = false;
-          break;
-        }
+        if (lane == 0) mbar_arrive(&d_ready[buf]);
+      };
+      auto epilogue = [&](int r) -> bool {
+        const int64_t g = g0 + r;
+        const int buf = static_cast<int>(g & 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&mma_done[buf], static_cast<uint32_t>((g >> 1) & 1)))) return false;
         tc_fence_after();
 #pragma unroll 1
         for (int cl = 0; cl < kHtRound; ++cl) {
           const int c = r * kHtRound + cl;
           if (c >= cmax) break;
           float w[32];
-          tmem_ld_32x32b_x32(tl + static_cast<uint32_t>((cl * kHtCols + col) * 32), w);
+          tmem_ld_32x32b_x32(tl + buf * kHtTmemBuf + static_cast<uint32_t>((cl * kHtCols + col) * 32), w);
           if (!(fast && c < ncand)) continue;
-          const uint32_t src = my_d + cl * kHtCols * kHtDBytes;
+          const uint32_t src = my_d + buf * kHtDBuf + cl * kHtCols * kHtDBytes;
           float e_sc, a_sc;
           if (use_cs) {
             ht_epilogue<true>(w, src, r_tile, cb, e_sc, a_sc);
@@ -1659,7 +1675,18 @@ __global__ void __launch_bounds__(kHtThreads, 2)
           }
         }
         tc_fence_before();
+        return true;
+      };
+      form(0);
+      if (n_rounds > 1) form(1);
+      for (int r = 0; r < n_rounds; ++r) {
+        if (!epilogue(r)) {
+          ok = false;
+          break;
+        }
+        if (r + 2 < n_rounds) form(r + 2);
       }
+      round = g0 + n_rounds;
       if (!ok) break;
       // Decided when every other candidate's lower end clears the best's upper end.
       const bool decided = fast && !bad && runner > __fadd_ru(best, best_tol);
