@@ -450,9 +450,26 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
   bool rare = false;  // FAST only: a candidate e >= 126 -> left for quantize_fixup_kernel
   if constexpr (OBJ == kObjRtn) {
     // core.py:240-243: the exponent is clamped to [-127, 127] before storage.
-    raw = max(-127, min(127, rtn_exponent(B.amax)));
+    // An infinite maximum gives log2 = inf there, clamped to 127; a NaN
+    // maximum fails the `> 0` test and gives -127 (rtn_exponent).
+    raw = isinf(B.amax) ? 127 : max(-127, min(127, rtn_exponent(B.amax)));
   } else {
     float anchor = block_anchor<QM>(B.amax, B.second, B.nt2, P);
+    // Non-finite blocks, as the reference's float arithmetic takes them
+    // (core.py:183-249): torch.quantile is NaN when the block holds a NaN, and
+    // its lerp turns an infinity into NaN for w >= 0.5.  A NaN anchor makes
+    // every candidate NaN, so the exponent stays NaN: its E8M0 byte is the
+    // x86 float->uint8 conversion of NaN (0) and every scaled value is NaN,
+    // which the bucket search maps to code 7 with no sign.  An infinite anchor
+    // makes every candidate +inf, clamped to 127.
+    if (isnan(B.amax) || isnan(anchor)) {
+      packed = make_uint4(0x77777777u, 0x77777777u, 0x77777777u, 0x77777777u);
+      return 0u;
+    }
+    if (isinf(anchor)) {
+      encode_block(B, P, 127, packed);
+      return 254u;
+    }
     const bool near_zero = B.amax < 1e-6f;
     anchor = fmaxf(anchor, 1e-6f);
     const int floor_e = floor_log2_div6(anchor);
@@ -499,6 +516,23 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
     }
   }
   encode_block(B, P, raw, packed);
+  if constexpr (OBJ == kObjRtn) {
+    if (isnan(B.amax)) {
+      // NaN elements of an rtn block: the reference's bucket search puts a NaN
+      // in bucket 7 and its sign test (x < 0) is false, so the code is 7
+      // whatever the hardware conversion does with a NaN.
+      uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const f2 v = unpack2(B.signed_pair(j));
+        uint32_t& word = w[j >> 2];
+        const int sh = 8 * (j & 3);
+        if (isnan(v.x)) word = (word & ~(0xfu << sh)) | (0x7u << sh);
+        if (isnan(v.y)) word = (word & ~(0xf0u << sh)) | (0x70u << sh);
+      }
+      packed = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
   return rare ? kRareBlock : static_cast<uint32_t>(raw + 127);
 }
 

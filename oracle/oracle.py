@@ -75,12 +75,19 @@ def quantize_mxfp4(
     method: str = "mse",
     mse_clip_depth: int = 1,
     *,
-    dtype: str = "bf16",
+    dtype: str | None = None,
     threads: int | None = None,
 ) -> tuple[np.ndarray, np.ndarray]:
-    """Oracle quantize.  ``weight`` is uint16 bf16/f16 bits or float32, [R, K]."""
+    """Oracle quantize.  ``weight`` is uint16 bf16/f16 bits or float32, [R, K].
+
+    ``dtype`` defaults to "f32" for a float32 array and "bf16" for uint16 bits
+    (f16 bits need ``dtype="f16"``)."""
     lib = _load()
     w = np.ascontiguousarray(weight)
+    if dtype is None:
+        dtype = "f32" if w.dtype == np.float32 else "bf16"
+    if (dtype == "f32") != (w.dtype == np.float32):
+        raise ValueError(f"weight dtype {w.dtype} does not match dtype={dtype!r}")
     if w.ndim != 2:
         raise ValueError("oracle expects a 2-D weight")
     rows, cols = w.shape

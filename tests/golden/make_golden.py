@@ -4,6 +4,7 @@ Run in a container where the reference MxWave checkout is importable:
 
     python tests/golden/make_golden.py --reference /path/to/MxWave
     python tests/golden/make_golden.py --reference /path/to/MxWave --only-layers
+    python tests/golden/make_golden.py --reference /path/to/MxWave --only-nonfinite
 
 It imports the reference's own ``mxwave.core.quantize_mxfp4`` and
 ``mxwave.calibration.ActivationCollector`` (CPU, fp32) and records:
@@ -20,6 +21,9 @@ It imports the reference's own ``mxwave.core.quantize_mxfp4`` and
 
 Weights are quantized through the reference's ``iter_quantized_row_chunks``
 with its default 1,048,576-element chunks, as its engine does.
+
+``--only-nonfinite`` runs ``nonfinite_golden.py``: blocks holding NaN or
+infinity, every objective.
 
 ``--only-layers`` runs ``layer_golden.py``: the decoder-layer workload (the
 reference's sequential calibration of a random-init layer, then all seven
@@ -104,8 +108,15 @@ def main() -> None:
     ap.add_argument("--skip-configs", action="store_true")
     ap.add_argument("--only-layers", action="store_true",
                     help="only (re)generate the decoder-layer and expert-stack fixtures (configs 4 and 5)")
+    ap.add_argument("--only-nonfinite", action="store_true",
+                    help="only (re)generate the fixtures of blocks holding NaN or infinity")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
+    if args.only_nonfinite:
+        import nonfinite_golden
+
+        nonfinite_golden.main(HERE)
+        return
     if args.only_layers:
         import layer_golden
 

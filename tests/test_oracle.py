@@ -178,3 +178,26 @@ def test_oracle_matches_decoder_layer_reference_sha(short, objective) -> None:
     p, s = oracle.quantize_mxfp4(bits, mse_clip_depth=1, **kw)
     assert _sha(p) == cfg[key]["packed_sha256"]
     assert _sha(s) == cfg[key]["scales_sha256"]
+
+
+def _nonfinite_cases():
+    from pathlib import Path
+
+    from tests.golden import nonfinite_golden
+
+    here = Path(__file__).resolve().parent / "golden"
+    if not (here / "nonfinite.json").exists():
+        return []
+    return nonfinite_golden.load(here)[0]
+
+
+NONFINITE = _nonfinite_cases()
+
+
+@pytest.mark.parametrize("case", NONFINITE, ids=[c["name"] for c in NONFINITE])
+def test_oracle_matches_nonfinite_golden(case) -> None:
+    """Blocks holding NaN or infinity, against the reference's own bytes (nonfinite_golden.py)."""
+    p, s = oracle.quantize_mxfp4(case["weight"], **case["kwargs"])
+    np.testing.assert_array_equal(s, case["scales"])
+    np.testing.assert_array_equal(p, case["packed"])
+

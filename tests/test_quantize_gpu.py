@@ -206,6 +206,32 @@ def test_nonfinite_input_sets_flag(cuda_device) -> None:
     assert int(flags.item()) & _lib.MXW_FLAG_NONFINITE
 
 
+def _nonfinite_cases():
+    from pathlib import Path
+
+    from tests.golden import nonfinite_golden
+
+    here = Path(__file__).resolve().parent / "golden"
+    if not (here / "nonfinite.json").exists():
+        return []
+    return nonfinite_golden.load(here)[0]
+
+
+NONFINITE = _nonfinite_cases()
+
+
+@pytest.mark.parametrize("case", NONFINITE, ids=[c["name"] for c in NONFINITE])
+def test_nonfinite_blocks_match_reference(case, cuda_device) -> None:
+    """NaN / infinity blocks through every kernel path (fast-path rare marker, Hessian
+    screening, rtn, fp32 inputs), against the reference's own bytes."""
+    w = case["weight"]
+    kw = {k: (torch.from_numpy(v).to(cuda_device) if isinstance(v, np.ndarray) else v)
+          for k, v in case["kwargs"].items()}
+    p, s = _gpu(_to_device(w, cuda_device, "f32" if w.dtype == np.float32 else "bf16"), cuda_device, **kw)
+    ref_w = w if w.dtype == np.float32 else syn.bf16_bits_to_f32(w)
+    assert_same_bytes(ref_w, p, s, case["packed"], case["scales"])
+
+
 def test_empty_and_argument_errors(cuda_device) -> None:
     p, s = quantize_mxfp4(torch.zeros((0, 64), dtype=torch.bfloat16, device=cuda_device))
     assert p.shape == (0, 32) and s.shape == (0, 2)
