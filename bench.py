@@ -600,10 +600,62 @@ def run_sweep(args, dev) -> dict:
         gbs = nbytes / (ms * 1e-3) / 1e9
         out[name] = {"us": round(ms * 1e3, 1), "algorithmic_GBps": round(gbs, 1), "frac": round(gbs / peak, 4),
                      "bf16_weight_GBps": round(INTER * HIDDEN * 2 / (ms * 1e-3) / 1e9, 1)}
+    del pk, sc, w, flush
     return {"workload": f"one {INTER} x {HIDDEN} bf16 weight per setting, pct {PCT} unless stated; Hessian blocks "
                         f"from the X^T X of {XTX_TOKENS} heavy-channel tokens",
             "peak_GBps": peak, "peak_kind": f"{peak_kind} copy bandwidth", "l2": "flushed before every launch",
-            "timing": "median of 9 single launches (main + rare-block pass), CUDA events", "settings": out}
+            "timing": "median of 9 single launches (main + rare-block pass), CUDA events", "settings": out,
+            "dense4096_graph64": _dense4096_graph(dev, peak)}
+
+
+def _dense4096_graph(dev, peak: float) -> dict:
+    """The dense 4096 x 4096 workload as 64 distinct weights quantized in one CUDA graph.
+
+    N(0, 0.02^2) with 0.1 % outliers x20 (the same law as the golden 4096^2
+    case), unweighted depth 1 and 4 and rtn; 2.1 GB of weights per replay, so
+    every launch reads from HBM.  Median of 5 replays.
+    """
+    import torch
+
+    from mxwave_b200 import synthetic
+    from mxwave_b200.core import quantize_into
+
+    n, k = 64, 4096
+    ws = [synthetic.torch_dense_weight(k, k, seed=700 + i, device=dev) for i in range(n)]
+    pk = torch.empty(k, k // 2, dtype=torch.uint8, device=dev)
+    sc = torch.empty(k, k // 32, dtype=torch.uint8, device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = {}
+    for name, kw in (("mse_d1", {}), ("mse_d4", {"mse_clip_depth": 4}), ("rtn", {"method": "rtn"})):
+        def batch(kw=kw) -> None:
+            for w in ws:
+                quantize_into(w, pk, sc, flags=flags, **kw)
+
+        batch()
+        torch.cuda.synchronize(dev)
+        side = torch.cuda.Stream(dev)
+        with torch.cuda.stream(side):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                batch()
+        torch.cuda.synchronize(dev)
+        graph.replay()
+        times = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        del graph
+        ms = sorted(times)[2]
+        nbytes = n * k * k * BYTES_PER_ELEM
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us_per_tensor": round(ms * 1e3 / n, 1), "algorithmic_GBps": round(gbs, 1),
+                     "frac": round(gbs / peak, 4), "bf16_weight_GBps": round(n * k * k * 2 / (ms * 1e-3) / 1e9, 1)}
+    del ws
+    return {"workload": f"{n} distinct {k} x {k} bf16 weights per CUDA graph replay", **out}
 
 
 LAYER_LINEARS = (("self_attn.q_proj", 5120), ("self_attn.k_proj", 5120), ("self_attn.v_proj", 5120),
@@ -1007,6 +1059,76 @@ def reference_python(seconds: float) -> dict:
                       f"({dt:.1f} s)"}
 
 
+def reference_python_workloads(seconds: float) -> dict:
+    """The reference's own Python on the host cores for the other workloads, each a bounded sample.
+
+    * dense 4096 x 4096 (unweighted, depth 1) through its chunk loop;
+    * block-Hessian depth 4 on rows of a 17408 x 5120 weight, Hessian blocks from
+      the reference collector on 1024 heavy-channel tokens;
+    * calibration: ActivationCollector.update (rms + block Hessian) and the fp32
+      X^T X (torch matmul, the product the reference does not form) on 4096 tokens.
+    """
+    import numpy as np
+    import torch
+
+    _reference_importable()
+    try:
+        from mxwave import calibration as ref_cal
+        from mxwave import checkpoint as ref_ckpt
+        from mxwave import core as ref_core
+    except ImportError:
+        return {"unavailable": "reference package not installed in baseline/_ref"}
+    from mxwave_b200 import synthetic
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+
+    def bf16(bits):
+        return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16)
+
+    def chunked(w, cols, **kw) -> float:
+        rows = w.shape[0]
+        t0 = time.perf_counter()
+        for _ in ref_ckpt.iter_quantized_row_chunks(
+                lambda a, b: w[a:b], lambda c: ref_core.quantize_mxfp4(c, **kw), rows=rows, columns=cols,
+                max_rows=1024, max_elements=ref_ckpt.DEFAULT_TENSOR_CHUNK_MAX_ELEMENTS, name="w"):
+            pass
+        return time.perf_counter() - t0
+
+    def sampled(bits, cols, **kw) -> tuple[int, float]:
+        w = bf16(bits)
+        probe = chunked(w[:256], cols, **kw)
+        rows = int(max(256, min(w.shape[0], 256 * seconds / max(probe, 1e-3))))
+        return rows, chunked(w[:rows], cols, **kw)
+
+    out = {"cores": threads, "kind": "reference"}
+    rows, dt = sampled(synthetic.det_dense_weight(4096, 4096, seed=0), 4096)
+    out["dense4096_mse_d1"] = {"value": round(rows * 4096 * 2 / dt / 1e9, 4), "unit": "GB/s",
+                               "sample": f"{rows} of 4096 rows ({dt:.1f} s)"}
+    xb = bf16(synthetic.det_activations(1024, HIDDEN, seed=300))
+    col = ref_cal.ActivationCollector({"w.weight": HIDDEN}, ("block-hessian",))
+    col.update("w.weight", xb)
+    hess = col.finalize()["block-hessian"]["w.weight"]
+    rows, dt = sampled(synthetic.det_dense_weight(INTER, HIDDEN, seed=31, sigma=0.015), HIDDEN, hessian=hess,
+                       mse_clip_depth=4)
+    out["hessian_d4"] = {"value": round(rows * HIDDEN * 2 / dt / 1e9, 4), "unit": "GB/s",
+                         "sample": f"{rows} of {INTER} rows x {HIDDEN} ({dt:.1f} s)"}
+    n = 4096
+    xc = bf16(synthetic.det_activations(n, HIDDEN, seed=2))
+    col = ref_cal.ActivationCollector({"w.weight": HIDDEN}, ("rms", "block-hessian"))
+    t0 = time.perf_counter()
+    col.update("w.weight", xc)
+    dt_col = time.perf_counter() - t0
+    xf = xc.float()
+    t0 = time.perf_counter()
+    _ = xf.T @ xf
+    dt_xtx = time.perf_counter() - t0
+    out["collector_update_tokens_per_s"] = round(n / dt_col, 1)
+    out["xtx_fp32_tokens_per_s"] = round(n / dt_xtx, 1)
+    out["calibration_sample"] = f"{n} x {HIDDEN} bf16 tokens"
+    return out
+
+
 def run_reference(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1033,6 +1155,7 @@ def run_reference(args) -> None:
     value = elems * 2 * args.steps / dt / 1e9
     sample = f"the whole workload: {N_WEIGHTS} x {rows} rows x {HIDDEN} per step"
     py = None if args.no_reference_python else reference_python(args.cpu_seconds)
+    py_more = None if args.no_reference_python else reference_python_workloads(args.cpu_seconds / 3)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -1051,6 +1174,7 @@ def run_reference(args) -> None:
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "reference_python": py,
+        "reference_python_workloads": py_more,
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
