@@ -1289,7 +1289,10 @@ constexpr int kHtDBuf = kHtRound * kHtCols * kHtDBytes;    // one round's D
 constexpr int kHtOffH = kHtOffD + kHtBufs * kHtDBuf;
 constexpr int kHtOffB = kHtOffH + kHtCols * 2 * kHtHBytes;
 constexpr int kHtOffBar = kHtOffB + kHtCols * 68 * 4;
-constexpr size_t kHtSmem = 1024 + kHtOffBar + (2 * kHtStages + 2 * kHtBufs + 1) * 8 + 16;
+// Output hand-off slots [quarter][lane]: 16 packed bytes, then the scale byte (after the barriers
+// and the TMEM slot).
+constexpr int kHtOffPair = (kHtOffBar + (2 * kHtStages + 2 * kHtBufs + 9) * 8 + 16 + 15) & ~15;
+constexpr size_t kHtSmem = 1024 + kHtOffPair + 4 * 32 * 16 + 4 * 32 * 4;
 
 // Byte offset of row r's 16-byte chunk kc (elements 8kc .. 8kc+7) in a K-major
 // no-swizzle operand of K = 32: 8-row x 16-byte core matrices, 128 bytes
@@ -1401,7 +1404,11 @@ __global__ void __launch_bounds__(kHtThreads, 2)
   uint64_t* d_ready = empty + kHtStages;    // [kHtBufs]: a round's D is in shared memory
   uint64_t* mma_done = d_ready + kHtBufs;   // [kHtBufs]: a round's products are in TMEM
   uint64_t* strip_bar = mma_done + kHtBufs;  // the consumer warps' barrier around a block-column change
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(strip_bar + 1);
+  uint64_t* pair_ready = strip_bar + 1;       // [4]: a column-1 warp's output half is staged
+  uint64_t* pair_free = pair_ready + 4;       // [4]: the column-0 warp has taken it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair_free + 4);
+  uint4* pair_pk = reinterpret_cast<uint4*>(smem + kHtOffPair);                      // [4][32]
+  uint32_t* pair_sc = reinterpret_cast<uint32_t*>(smem + kHtOffPair + 4 * 32 * 16);  // [4][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_strips = (P.nb + kHtCols - 1) / kHtCols;
@@ -1421,6 +1428,10 @@ __global__ void __launch_bounds__(kHtThreads, 2)
       mbar_init(&mma_done[b], 1);
     }
     mbar_init(strip_bar, kHtConsumerWarps);
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(&pair_ready[q], 1);
+      mbar_init(&pair_free[q], 1);
+    }
     fence_mbar_init();
   }
   if (warp == kHtMmaWarp) tmem_alloc(tmem_slot, kHtTmemCols);
@@ -1736,10 +1747,52 @@ __global__ void __launch_bounds__(kHtThreads, 2)
         sc = kRareBlock;
       }
       if (active) {
-        *reinterpret_cast<uint4*>(P.packed + row * (P.cols / 2) + b * 16) = pk;
-        P.scales[row * P.nb + b] = static_cast<uint8_t>(sc);
         any_nonfinite |= nonfinite;
         any_rare |= sc == kRareBlock;
+      }
+      // Output.  A row's two block columns are adjacent 16-byte halves of one
+      // 32-byte sector and two adjacent scale bytes: the column-1 warp of each
+      // row quarter hands its half to the column-0 warp through shared memory,
+      // and that warp writes both (half the store transactions, no partial
+      // packed sectors).  Both hand-off waits are bounded.
+      const int slot = quarter * 32 + lane;
+      if (col == 1) {
+        if (i > 0 && !__all_sync(0xffffffffu, mbar_wait(&pair_free[quarter], static_cast<uint32_t>((i - 1) & 1)))) {
+          ok = false;
+          break;
+        }
+        pair_pk[slot] = pk;
+        pair_sc[slot] = sc;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pair_ready[quarter]);
+      } else {
+        if (!__all_sync(0xffffffffu, mbar_wait(&pair_ready[quarter], static_cast<uint32_t>(i & 1)))) {
+          ok = false;
+          break;
+        }
+        const uint4 pk1 = pair_pk[slot];
+        const uint32_t sc1 = pair_sc[slot];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pair_free[quarter]);
+        if (active) {
+          const bool both = b + 1 < P.nb;
+          uint8_t* dst = P.packed + row * (P.cols / 2) + b * 16;
+          if (both && (reinterpret_cast<uintptr_t>(dst) & 31u) == 0) {
+            asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(pk.x), "r"(pk.y),
+                         "r"(pk.z), "r"(pk.w), "r"(pk1.x), "r"(pk1.y), "r"(pk1.z), "r"(pk1.w)
+                         : "memory");
+          } else {
+            *reinterpret_cast<uint4*>(dst) = pk;
+            if (both) *reinterpret_cast<uint4*>(dst + 16) = pk1;
+          }
+          uint8_t* sdst = P.scales + row * P.nb + b;
+          if (both && (reinterpret_cast<uintptr_t>(sdst) & 1u) == 0) {
+            *reinterpret_cast<uint16_t*>(sdst) = static_cast<uint16_t>((sc & 0xffu) | ((sc1 & 0xffu) << 8));
+          } else {
+            sdst[0] = static_cast<uint8_t>(sc);
+            if (both) sdst[1] = static_cast<uint8_t>(sc1);
+          }
+        }
       }
     }
     if (P.flags && __any_sync(0xffffffffu, any_nonfinite) && lane == 0) atomicOr(P.flags, MXW_FLAG_NONFINITE);
