@@ -787,6 +787,39 @@ __device__ __forceinline__ float one_candidate_error(const unsigned long long (&
   return __fmul_rn(acc, 0.03125f);
 }
 
+// Error of candidate e for the block of lane `src`, by the whole warp: lane l
+// takes element l (staged through the warp's 32-float scratch `Xw`) and forms
+// fl(fl(t - q*2^e)^2 [* gamma^2]) as one_candidate_error does; the lane
+// partials ((x_l + x_{l+8}) + x_{l+16}) + x_{l+24} and their left-to-right sum
+// are the reference's 8-lane order.  Warp-collective; every lane gets the error.
+template <bool GAMMA>
+__device__ __forceinline__ float warp_candidate_error(const unsigned long long (&t2)[16], int e, int src, int lane,
+                                                      const float* Gw, float* Xw, const QuantParams& P) {
+  __syncwarp();
+  if (lane == src) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) reinterpret_cast<unsigned long long*>(Xw)[j] = t2[j];
+  }
+  __syncwarp();
+  const float t = Xw[lane];
+  const float x = __fmaf_rn(t, exp2i(-e), P.zero);
+  uint32_t h2;
+  asm("{\n\t.reg .b8 c;\n\tcvt.rn.satfinite.e2m1x2.f32 c, %1, %2;\n\tcvt.rn.f16x2.e2m1x2 %0, c;\n\t}"
+      : "=r"(h2) : "f"(0.0f), "f"(x));
+  const float q = __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xffffu)));
+  const float d = __fmaf_rn(q, -exp2i(e), t);
+  float sq = __fmul_rn(d, d);
+  if constexpr (GAMMA) sq = __fmul_rn(sq, Gw[lane]);
+  float part = __fadd_rn(sq, __shfl_down_sync(0xffffffffu, sq, 8));
+  part = __fadd_rn(part, __shfl_down_sync(0xffffffffu, sq, 16));
+  part = __fadd_rn(part, __shfl_down_sync(0xffffffffu, sq, 24));
+  float acc = __shfl_sync(0xffffffffu, part, 0);
+#pragma unroll
+  for (int l = 1; l < 8; ++l) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, part, l));
+  __syncwarp();  // Xw is reused by the next block
+  return __fmul_rn(acc, 0.03125f);
+}
+
 // Warp-collective (the extra candidates run under warp votes): every lane
 // calls it; `active` marks lanes whose tile row exists.  Reads its block (tile
 // row `lane`, block column w) from the stage; lane 0 releases the stage on
@@ -794,7 +827,7 @@ __device__ __forceinline__ float one_candidate_error(const unsigned long long (&
 // kRareBlock) and the packed codes; `nonfinite` reports NaN/inf.
 template <int DT, int OBJ, int QM>
 __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const QuantParams& P, const uint8_t* stage,
-                                                        int w, int lane, const float* Gw, const uint32_t* G2b,
+                                                        int w, int lane, const float* Gw, float* Xw, const uint32_t* G2b,
                                                         uint64_t* release, uint4& packed, bool& nonfinite) {
   constexpr bool GAMMA = OBJ == kObjGamma;
   float amax, second;
@@ -913,9 +946,16 @@ __device__ __forceinline__ uint32_t quantize_block_fast(bool active, const Quant
     const float lb = __fmul_rn(__fmul_rn(__fadd_rn(a2.x, a2.y), exp2i(2 * f + 2)), 0.03125f);
     run_safe = run_safe && !lb_prunes(lb, best);
   }
-  if (__any_sync(0xffffffffu, run_safe)) {
-    const float err = one_candidate_error<GAMMA>(t2, safe_e, Gw, P);
-    if (run_safe && err < best) raw = safe_e;
+  // The safe candidate is needed by a few scattered blocks (about 2 % with
+  // gamma weights, but then in half of the warps): each such block is
+  // evaluated by the whole warp, lane = element, instead of by its thread
+  // with the other 31 lanes idle.
+  uint32_t need = __ballot_sync(0xffffffffu, run_safe);
+  while (need) {
+    const int src = __ffs(need) - 1;
+    need &= need - 1;
+    const float err = warp_candidate_error<GAMMA>(t2, __shfl_sync(0xffffffffu, safe_e, src), src, lane, Gw, Xw, P);
+    if (lane == src && err < best) raw = safe_e;
   }
 
   if (near_zero && active && !nonfinite) {
@@ -962,8 +1002,9 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   uint8_t* scale_stage = out_stage + kOutBuffers * kOutTileBytes;  // [ring][32 rows][8 B]
   float* Hs = reinterpret_cast<float*>(scale_stage + kOutBuffers * kScaleTileBytes);
   float* Gs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(Hs) + (OBJ == kObjHess ? kTileBlocks * 1024 * 4 : 0));
-  uint64_t* full =
-      reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(Gs) + (OBJ == kObjGamma ? kTileBlocks * kGammaWords * 4 : 0));
+  // One block's 32 elements per consumer warp, for the warp-cooperative candidate evaluation.
+  float* Xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(Gs) + (OBJ == kObjGamma ? kTileBlocks * kGammaWords * 4 : 0));
+  uint64_t* full = reinterpret_cast<uint64_t*>(Xs + kTileBlocks * kBlock);
   uint64_t* empty = full + kStages;
   uint64_t* out_full = empty + kStages;
   uint64_t* out_empty = out_full + kOutBuffers;
@@ -1097,7 +1138,7 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
         // Warp-collective; the stage stays held until its warp evaluation is done.
         // Warp-collective; it releases the stage once the warp has read it.
         bool nf = false;
-        sc = quantize_block_fast<DT, OBJ, QM>(active, P, stages + s * kStageBytes, warp, lane, Gw,
+        sc = quantize_block_fast<DT, OBJ, QM>(active, P, stages + s * kStageBytes, warp, lane, Gw, Xs + warp * kBlock,
                                               reinterpret_cast<const uint32_t*>(Gw + kBlock), &empty[s], pk, nf);
         any_nonfinite |= active && nf;
       } else {
@@ -2039,7 +2080,7 @@ template <int DT, int OBJ, int QM>
 static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStream_t stream) {
   const size_t smem = 1024 + kStages * Elem<DT>::kStageBytes + kOutBuffers * (kOutTileBytes + kScaleTileBytes) +
                       (OBJ == kObjHess ? kTileBlocks * 4096 : 0) + (OBJ == kObjGamma ? kTileBlocks * kGammaWords * 4 : 0) +
-                      (2 * kStages + 2 * kOutBuffers) * sizeof(uint64_t);
+                      kTileBlocks * kBlock * 4 + (2 * kStages + 2 * kOutBuffers) * sizeof(uint64_t);
   CUtensorMap map;
   const CUtensorMapDataType dt = DT == MXW_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : DT == MXW_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
