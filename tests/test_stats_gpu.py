@@ -174,10 +174,12 @@ def test_xtx_matches_fp64(tokens, cols, cuda_device) -> None:
     assert np.array_equal(got, got.T)
 
 
-@pytest.mark.parametrize("cols", [384, 640])
+@pytest.mark.parametrize("cols", [384, 512, 640, 1024])
 def test_xtx_packed_then_unpacked_equals_direct(cols, cuda_device) -> None:
     """Two token slices accumulated in the packed tile form and unpacked give
-    the direct path's Gram bit for bit (the all-reduce path of the bench)."""
+    the direct path's Gram bit for bit (the all-reduce path of the bench).
+    Widths that are a multiple of 256 run on CTA pairs, the others on single
+    CTAs; both write the same packed tile layout."""
     lib = _lib.load()
     x, _ = _x(3000, cols, cols + 5, cuda_device)
     direct = torch.zeros(cols, cols, device=cuda_device)
