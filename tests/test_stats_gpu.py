@@ -177,9 +177,8 @@ def test_xtx_matches_fp64(tokens, cols, cuda_device) -> None:
 @pytest.mark.parametrize("cols", [384, 512, 640, 1024])
 def test_xtx_packed_then_unpacked_equals_direct(cols, cuda_device) -> None:
     """Two token slices accumulated in the packed tile form and unpacked give
-    the direct path's Gram bit for bit (the all-reduce path of the bench).
-    Widths that are a multiple of 256 run on CTA pairs, the others on single
-    CTAs; both write the same packed tile layout."""
+    the direct path's Gram bit for bit (the all-reduce path of the bench), at
+    widths with and without a ragged last 256-column tile."""
     lib = _lib.load()
     x, _ = _x(3000, cols, cols + 5, cuda_device)
     direct = torch.zeros(cols, cols, device=cuda_device)
