@@ -253,6 +253,182 @@ __global__ void __launch_bounds__(kStatThreads, GRAM ? 2 : 3)
   cluster_sync_all();
 }
 
+// ------------------------------------------------ moments-only pass
+//
+// Per-channel sum |x| and / or sum x^2 without the block Gram.  This pass is
+// pure streaming, so it reads X straight from global memory with 8-byte
+// (2-byte types) or 16-byte (fp32) vector loads: every warp load covers one
+// whole 256- or 512-byte row segment, with no shared-memory staging.  A
+// thread-block cluster owns a 128-channel strip and CTA rank r streams token
+// slice r of it.  Warp w takes rows w, w + 8, ... of the slice and lane l
+// channels 4l .. 4l + 3, with 16 rows in flight per lane (a batch).  Each
+// batch is summed in fp32 and added into fp64 accumulators; the CTA folds its
+// eight warps in warp order and rank 0 folds the slices in rank order over
+// distributed shared memory, so the result is deterministic run to run.  Only
+// the requested sums are formed.
+
+constexpr int kMomStrip = 128;
+constexpr int kMomWarps = 8;
+constexpr int kMomBatch = 16;
+constexpr int kMomMaxSlices = 8;
+
+template <int DT>
+struct MomVec {  // four consecutive elements
+  using T = uint2;
+};
+template <>
+struct MomVec<MXW_F32> {
+  using T = uint4;
+};
+
+__device__ __forceinline__ void mom_load(const uint8_t* p, uint2& v) {
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+}
+__device__ __forceinline__ void mom_load(const uint8_t* p, uint4& v) {
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+}
+
+template <int DT>
+__device__ __forceinline__ void mom_unpack(const typename MomVec<DT>::T& v, float (&x)[4]) {
+  if constexpr (DT == MXW_BF16) {
+    x[0] = bits_f32(v.x << 16);
+    x[1] = bits_f32(v.x & 0xffff0000u);
+    x[2] = bits_f32(v.y << 16);
+    x[3] = bits_f32(v.y & 0xffff0000u);
+  } else if constexpr (DT == MXW_F16) {
+    const __half2 a = *reinterpret_cast<const __half2*>(&v.x), b = *reinterpret_cast<const __half2*>(&v.y);
+    x[0] = __low2float(a);
+    x[1] = __high2float(a);
+    x[2] = __low2float(b);
+    x[3] = __high2float(b);
+  } else {
+    x[0] = __uint_as_float(v.x);
+    x[1] = __uint_as_float(v.y);
+    x[2] = __uint_as_float(v.z);
+    x[3] = __uint_as_float(v.w);
+  }
+}
+
+struct MomParams {
+  const uint8_t* x;
+  int64_t ld_bytes, tokens, cols;
+  float* sum_abs;
+  float* sum_sq;
+};
+
+template <int DT, bool ABS, bool SQ>
+__global__ void __launch_bounds__(kMomWarps * 32, 3) moments_kernel(const MomParams P) {
+  using V = typename MomVec<DT>::T;
+  constexpr int EB = StatElem<DT>::kBytes;
+  __shared__ double red[kMomWarps][kMomStrip][2];  // each warp's accumulators (16 KB)
+  __shared__ double part[kMomStrip][2];            // this CTA's slice totals, read by rank 0
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned rank = cluster.block_rank(), nrank = cluster.num_blocks();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * kMomStrip + 4 * lane;  // this lane's first channel
+  const bool have = c < P.cols;  // cols % 4 == 0: all four channels or none
+  const int64_t r0 = P.tokens * rank / nrank, r1 = P.tokens * (rank + 1) / nrank;
+  const uint8_t* base = P.x + c * EB;
+  double da[4] = {0.0, 0.0, 0.0, 0.0}, dq[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int64_t r = r0 + warp; r < r1; r += kMomWarps * kMomBatch) {
+    V v[kMomBatch];
+#pragma unroll
+    for (int k = 0; k < kMomBatch; ++k) {
+      const int64_t rr = r + k * kMomWarps;
+      if (have && rr < r1) {
+        mom_load(base + rr * P.ld_bytes, v[k]);
+      } else {
+        v[k] = V{};
+      }
+    }
+    float fa[4] = {0.f, 0.f, 0.f, 0.f}, fq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < kMomBatch; ++k) {
+      float x[4];
+      mom_unpack<DT>(v[k], x);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if constexpr (ABS) fa[j] = __fadd_rn(fa[j], fabsf(x[j]));
+        if constexpr (SQ) fq[j] = __fmaf_rn(x[j], x[j], fq[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      da[j] += fa[j];
+      dq[j] += fq[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    red[warp][4 * lane + j][0] = da[j];
+    red[warp][4 * lane + j][1] = dq[j];
+  }
+  __syncthreads();
+  if (threadIdx.x < kMomStrip) {
+    double a = 0.0, q = 0.0;
+    for (int w = 0; w < kMomWarps; ++w) {
+      a += red[w][threadIdx.x][0];
+      q += red[w][threadIdx.x][1];
+    }
+    part[threadIdx.x][0] = a;
+    part[threadIdx.x][1] = q;
+  }
+  // Every thread of every CTA of the cluster reaches both cluster barriers
+  // exactly once (no waits above), so neither waits forever.
+  cluster_sync_all();
+  if (rank == 0 && threadIdx.x < kMomStrip) {
+    const int64_t ch = static_cast<int64_t>(blockIdx.x) * kMomStrip + threadIdx.x;
+    if (ch < P.cols) {
+      double a = 0.0, q = 0.0;
+      for (unsigned s = 0; s < nrank; ++s) {
+        const double* pp = cluster.map_shared_rank(&part[0][0], s);
+        a += pp[2 * threadIdx.x];
+        q += pp[2 * threadIdx.x + 1];
+      }
+      if constexpr (ABS) P.sum_abs[ch] += static_cast<float>(a);
+      if constexpr (SQ) P.sum_sq[ch] += static_cast<float>(q);
+    }
+  }
+  // Keep every CTA's shared memory alive until rank 0 has read it.
+  cluster_sync_all();
+}
+
+// Token slices per strip (the cluster size): about 512 tokens or more each,
+// at most kMomMaxSlices.
+static int mom_slices(int64_t tokens) {
+  return static_cast<int>(std::min<int64_t>(kMomMaxSlices, std::max<int64_t>(1, tokens / 512)));
+}
+
+template <int DT, bool ABS, bool SQ>
+static int launch_moments(const void* x, int64_t ld, const StatParams& P, cudaStream_t stream) {
+  MomParams Q{static_cast<const uint8_t*>(x), ld * StatElem<DT>::kBytes, P.tokens, P.cols, P.sum_abs, P.sum_sq};
+  const int S = mom_slices(P.tokens);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((P.cols + kMomStrip - 1) / kMomStrip), static_cast<unsigned>(S), 1);
+  cfg.blockDim = dim3(kMomWarps * 32, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(S);
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, moments_kernel<DT, ABS, SQ>, Q);
+  if (err != cudaSuccess) return record_cuda_error(err);
+  return check_launch();
+}
+
+template <int DT>
+static int launch_moments_any(const void* x, int64_t ld, const StatParams& P, cudaStream_t stream) {
+  if (P.sum_abs && P.sum_sq) return launch_moments<DT, true, true>(x, ld, P, stream);
+  if (P.sum_abs) return launch_moments<DT, true, false>(x, ld, P, stream);
+  return launch_moments<DT, false, true>(x, ld, P, stream);
+}
+
 // Plain-load fallback (unaligned base or row stride): one thread per channel
 // for the moments, one thread per Gram element.
 template <int DT>
@@ -346,6 +522,12 @@ static int launch_stats(const void* x, int64_t ld, const StatParams& P, bool mom
     return check_launch();
   }
   if (moments && gram) return launch_stats_tma<DT, true, true>(x, ld, P, stream);
+  // Moments only: the vector-load pass when every lane's four channels are
+  // aligned (8-byte loads for 2-byte types, 16-byte for fp32).
+  constexpr int64_t kVecBytes = DT == MXW_F32 ? 16 : 8;
+  if (moments && P.cols % 4 == 0 && reinterpret_cast<uintptr_t>(x) % kVecBytes == 0 &&
+      (ld * StatElem<DT>::kBytes) % kVecBytes == 0)
+    return launch_moments_any<DT>(x, ld, P, stream);
   if (moments) return launch_stats_tma<DT, true, false>(x, ld, P, stream);
   return launch_stats_tma<DT, false, true>(x, ld, P, stream);
 }

@@ -62,6 +62,35 @@ def test_moments_and_block_gram(tokens, cols, dtype, cuda_device) -> None:
     assert _gram_err(g.cpu().numpy(), oracle.block_gram(xf)) < RTOL
 
 
+# Moments without the block Gram take the vector-load pass when the width is a
+# multiple of 4 and the rows are 8-byte aligned (16-byte for fp32): 128-channel
+# strips (the last one ragged below), one to eight token slices per strip.
+@pytest.mark.parametrize("tokens,cols", [(1, 4), (513, 100), (9000, 644), (4096, 5120)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("which", ["abs", "sq", "both"])
+def test_moments_only_pass(tokens, cols, dtype, which, cuda_device) -> None:
+    lib = _lib.load()
+    x, xf = _x(tokens, cols, 7 * tokens + cols, cuda_device, dtype)
+    code = {torch.bfloat16: _lib.MXW_BF16, torch.float16: _lib.MXW_F16, torch.float32: _lib.MXW_F32}[dtype]
+    r1, r2 = oracle.moments(xf)
+    runs = []
+    for _ in range(2):
+        s1 = torch.full((cols,), 0.5, device=cuda_device) if which != "sq" else None
+        s2 = torch.full((cols,), 0.25, device=cuda_device) if which != "abs" else None
+        st = lib.mxw_accumulate_moments(x.data_ptr(), code, tokens, cols, cols,
+                                        None if s1 is None else s1.data_ptr(),
+                                        None if s2 is None else s2.data_ptr(), _stream(cuda_device))
+        assert st == _lib.MXW_OK
+        torch.cuda.synchronize()
+        if s1 is not None:
+            np.testing.assert_allclose(s1.cpu().numpy(), r1 + 0.5, rtol=RTOL)
+        if s2 is not None:
+            np.testing.assert_allclose(s2.cpu().numpy(), r2 + 0.25, rtol=RTOL)
+        runs.append([t.cpu() for t in (s1, s2) if t is not None])
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)  # fixed summation order: identical bits run to run
+
+
 # Widths that are multiples of 128 with 2-byte activations take the tensor-core
 # block Gram (xtx.cu block_gram_tc_kernel): one to eight token slices per
 # 128-channel strip, and more than one launch past 262,144 tokens.
