@@ -47,7 +47,7 @@ METRIC = "bf16 weight GB/s quantized"
 # profiles/quantize_tma_kernel_gamma_d1_17408x5120.txt (178.37 MB + 26.45 MB).
 QUANT_TRAFFIC_BYTES = 178_365_184 + 26_449_920
 # The same for one X^T X launch (profiles/xtx_kernel_full_gram_65536x5120.txt).
-XTX_TRAFFIC_BYTES = 1_693_721_000 + 90_838_528
+XTX_TRAFFIC_BYTES = 1_682_721_000 + 92_257_536
 
 
 def _peaks() -> tuple[float, str]:
