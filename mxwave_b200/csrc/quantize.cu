@@ -71,9 +71,6 @@ extern "C" int mxw_quantize_mxfp4(const void* weight, int dtype, int64_t rows, i
   P.scales = scales;
   P.flags = flags;
   P.depth = mse_clip_depth;
-  // Row-major tiles for gamma weights with two or more clipping candidates
-  // (the measurement is beside TileOrder); strip-major otherwise.
-  P.row_order = (gamma && !hessian && mse_clip_depth >= 2) ? 1 : 0;
   P.zero = 0.0f;
   P.negzero = -0.0f;
   // torch.quantile(|b|, p/100) over 32 values: ranks = fp32(p/100) * 31,

@@ -47,7 +47,6 @@ struct QuantParams {
   uint8_t* scales;
   uint32_t* flags;
   int depth;
-  int row_order;  // quantize_tma_kernel tile order: 1 row-major, 0 strip-major (see TileOrder)
   int q_below, q_above, q_small;
   float q_w;
   // Always 0.0f.  Added to the scaled values before encoding so that -0
@@ -541,20 +540,6 @@ __device__ __forceinline__ uint32_t quantize_one_block(const BlockData<DT>& B, c
 // values as bf16x2 pairs for the clipping bound) or the block Hessian.
 constexpr int kGammaWords = kBlock + kBlock / 2;
 
-// gamma -> the warp's gamma^2 state (lane = column of the block).
-__device__ __forceinline__ void store_gamma_state(float g, int lane, float* Gw) {
-  __syncwarp();
-  const float g2 = __fmul_rn(g, g);
-  Gw[lane] = g2;
-  const float g2n = __shfl_down_sync(0xffffffffu, g2, 1);
-  if ((lane & 1) == 0) {
-    uint32_t pr;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pr) : "f"(g2n), "f"(g2));
-    reinterpret_cast<uint32_t*>(Gw + kBlock)[lane >> 1] = pr;
-  }
-  __syncwarp();
-}
-
 template <int OBJ>
 __device__ __forceinline__ void load_column_state(const QuantParams& P, int64_t b, int lane, float* Hw, float* Gw) {
   if constexpr (OBJ == kObjGamma) {
@@ -1005,36 +990,7 @@ struct TileCursor {
   }
 };
 
-// The quantize kernel's tile order (ROW: QuantParams::row_order).
-// Strip-major keeps a CTA on one 256-column strip for many tiles, so a block
-// column's state is loaded once per strip.  Row-major runs across the strips
-// of a row of tiles, so every CTA's contiguous range holds the same mix of
-// strips: block columns whose blocks need several extra candidates
-// (heavy-gamma channels at depth >= 2) are spread over all CTAs instead of
-// slowing the few CTAs whose ranges lie in their strips.  It reloads the
-// gamma state every tile, from a value fetched one tile ahead.  Measured at
-// 17408 x 5120 bf16 with gamma weights: depth 4, 177 us row-major against
-// 187 us strip-major; depth 1, 138 us against 136 us, so the host picks
-// row-major only for gamma weights at depth >= 2.
-template <bool ROW>
-struct TileOrder {
-  int64_t strip, rt;
-  __device__ __forceinline__ TileOrder(int64_t t, int64_t n_row_tiles, int64_t n_strips)
-      : strip(ROW ? t % n_strips : t / n_row_tiles), rt(ROW ? t / n_strips : t % n_row_tiles) {}
-  __device__ __forceinline__ void advance(int64_t n_row_tiles, int64_t n_strips) {
-    if constexpr (ROW) {
-      if (++strip == n_strips) {
-        strip = 0;
-        ++rt;
-      }
-    } else if (++rt == n_row_tiles) {
-      rt = 0;
-      ++strip;
-    }
-  }
-};
-
-template <int DT, int OBJ, int QM, bool ROW>
+template <int DT, int OBJ, int QM>
 __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F32) ? 1 : 2)
     quantize_tma_kernel(const __grid_constant__ CUtensorMap map, const __grid_constant__ CUtensorMap out_map,
                         const QuantParams P) {
@@ -1058,8 +1014,6 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   // This CTA's contiguous range of tiles, strip-major.
   const int64_t t_begin = P.n_tiles * blockIdx.x / gridDim.x;
   const int64_t t_end = P.n_tiles * (blockIdx.x + 1) / gridDim.x;
-  const int64_t n_strips = P.n_tiles / P.n_row_tiles;
-  using Cursor = TileOrder<ROW>;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -1079,8 +1033,8 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
     bool ok = true;
     int64_t it = 0;
     const bool scale_words = (P.nb % 8 == 0) && (reinterpret_cast<uintptr_t>(P.scales) % 8 == 0);
-    Cursor cur(t_begin, P.n_row_tiles, n_strips);
-    for (int64_t t = t_begin; t < t_end; ++t, ++it, cur.advance(P.n_row_tiles, n_strips)) {
+    TileCursor cur(t_begin, P.n_row_tiles);
+    for (int64_t t = t_begin; t < t_end; ++t, ++it, cur.advance(P.n_row_tiles)) {
       const int64_t strip = cur.strip, rt = cur.rt;
       const int buf = static_cast<int>(it % kOutBuffers);
       if (!__all_sync(0xffffffffu, mbar_wait(&out_full[buf], static_cast<uint32_t>((it / kOutBuffers) & 1)))) {
@@ -1123,8 +1077,8 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
       prefetch_tensormap(&map);
       int64_t issued = 0;
       bool ok = true;
-      Cursor cur(t_begin, P.n_row_tiles, n_strips);
-      for (int64_t t = t_begin; t < t_end; ++t, ++issued, cur.advance(P.n_row_tiles, n_strips)) {
+      TileCursor cur(t_begin, P.n_row_tiles);
+      for (int64_t t = t_begin; t < t_end; ++t, ++issued, cur.advance(P.n_row_tiles)) {
         const int64_t strip = cur.strip, rt = cur.rt;
         const int64_t col0 = strip * kTileBlocks * kBlock;
         const int64_t left = (P.cols - col0 + Elem<DT>::kBoxCols - 1) / Elem<DT>::kBoxCols;
@@ -1158,33 +1112,14 @@ __global__ void __launch_bounds__(kQuantThreads, (OBJ == kObjHess || DT == MXW_F
   bool any_nonfinite = false;
   bool any_rare = false;  // a block marked kRareBlock: the rare-block pass has work
   int64_t it = 0;
-  Cursor cur(t_begin, P.n_row_tiles, n_strips);
-  // Row-major order changes strip every tile: the gamma of the next tile is
-  // loaded while the current one is quantized.  Strip-major order loads a
-  // strip's state when it starts.
-  constexpr bool kPrefetch = ROW && OBJ == kObjGamma;
-  float g_next = 0.0f;
-  if constexpr (kPrefetch) {
-    const int64_t bn = cur.strip * kTileBlocks + warp;
-    if (t_begin < t_end && bn < P.nb) g_next = __ldg(P.gamma + bn * kBlock + lane);
-  }
-  for (int64_t t = t_begin; t < t_end; ++t, ++it, cur.advance(P.n_row_tiles, n_strips)) {
+  TileCursor cur(t_begin, P.n_row_tiles);
+  for (int64_t t = t_begin; t < t_end; ++t, ++it, cur.advance(P.n_row_tiles)) {
     const int64_t strip = cur.strip, rt = cur.rt;
     if (strip != cur_strip) {
       cur_strip = strip;
       b = strip * kTileBlocks + warp;
       valid_col = b < P.nb;
-      if constexpr (kPrefetch) {
-        if (valid_col) store_gamma_state(g_next, lane, Gw);
-      } else {
-        if (valid_col) load_column_state<OBJ>(P, b, lane, Hw, Gw);
-      }
-    }
-    if constexpr (kPrefetch) {
-      Cursor nxt = cur;
-      nxt.advance(P.n_row_tiles, n_strips);
-      const int64_t bn = nxt.strip * kTileBlocks + warp;
-      if (t + 1 < t_end && bn < P.nb && nxt.strip != strip) g_next = __ldg(P.gamma + bn * kBlock + lane);
+      if (valid_col) load_column_state<OBJ>(P, b, lane, Hw, Gw);
     }
     const int s = static_cast<int>(it % kStages);
     // Warp-uniform verdict: a lane that timed out takes the whole warp out.
@@ -2157,10 +2092,7 @@ static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStre
   if (make_tensor_map_2d(&out_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, P0.packed, P0.cols / 2, P0.rows, P0.cols / 2,
                          kTileBlocks * 16, kTileRows, CU_TENSOR_MAP_SWIZZLE_128B) != MXW_OK)
     return MXW_ECUDA;
-  auto kern = quantize_tma_kernel<DT, OBJ, QM, false>;
-  if constexpr (OBJ == kObjGamma) {
-    if (P0.row_order) kern = quantize_tma_kernel<DT, OBJ, QM, true>;
-  }
+  auto kern = quantize_tma_kernel<DT, OBJ, QM>;
   int dev = 0;
   cudaGetDevice(&dev);
   LaunchInfo& li = launch_info(reinterpret_cast<const void*>(kern), dev);
@@ -2182,7 +2114,10 @@ static int launch_tma(const void* w, int64_t ld, const QuantParams& P0, cudaStre
   if constexpr (OBJ == kObjNone || OBJ == kObjGamma) {
     if (rc != MXW_OK) return rc;
     const int64_t chunks = (P.rows * P.nb + kFixupChunk - 1) / kFixupChunk;
-    const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()) * 2);
+    // One wave: at 255 registers a 256-thread CTA fills an SM, and the pass
+    // is a grid-stride loop, so a second wave only adds launch cost to the
+    // common case of a clear MXW_FLAG_RARE.
+    const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()));
     quantize_fixup_kernel<DT, OBJ, QM><<<static_cast<unsigned>(std::max<int64_t>(blocks, 1)), 256, 0, stream>>>(P, MXW_FLAG_RARE);
     return check_launch();
   }
@@ -2224,7 +2159,7 @@ static int launch_hess_tc(const void* w, int64_t ld, const QuantParams& P0, cuda
   if (rc2 != MXW_OK) return rc2;
   // Blocks with non-finite elements (returns at once when the main pass saw none).
   const int64_t chunks = (F.rows * F.nb + kFixupChunk - 1) / kFixupChunk;
-  const int64_t nf_blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()) * 2);
+  const int64_t nf_blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()));
   quantize_fixup_kernel<DT, kObjHess, QM><<<static_cast<unsigned>(std::max<int64_t>(nf_blocks, 1)), 256, 0, stream>>>(
       F, MXW_FLAG_NONFINITE);
   return check_launch();
