@@ -188,7 +188,10 @@ def _full_err(got: np.ndarray, ref: np.ndarray) -> float:
     return float(np.max(np.abs(got - ref) / scale))
 
 
-@pytest.mark.parametrize("tokens,cols", [(1, 128), (64, 128), (1000, 256), (300, 384), (4097, 640), (65536, 1024)])
+# 262,200 tokens: two launches (at most 262,144 tokens each) and a ragged last
+# 1024-token TMEM chunk.
+@pytest.mark.parametrize("tokens,cols", [(1, 128), (64, 128), (1000, 256), (300, 384), (4097, 640), (65536, 1024),
+                                         (262200, 128)])
 def test_xtx_matches_fp64(tokens, cols, cuda_device) -> None:
     lib = _lib.load()
     x, xf = _x(tokens, cols, tokens * 3 + cols, cuda_device)
