@@ -55,7 +55,7 @@ constexpr int kXtxBBytes = (kXtxBN / 64) * kXtxBoxBytes;      // 32 KB
 constexpr int kXtxStageBytes = kXtxABytes + kXtxBBytes;       // 48 KB
 constexpr int kXtxEpiWarps = 8;
 constexpr int kXtxThreads = (2 + kXtxEpiWarps) * 32;
-constexpr int kXtxChunkStages = 4;   // block Gram: 256 tokens per TMEM accumulation chunk
+constexpr int kXtxChunkStages = 16;  // block Gram: 1024 tokens per TMEM accumulation chunk
 constexpr int kXtxAccumStages = 16;  // full X^T X: 1024 tokens per TMEM accumulation chunk
 constexpr uint32_t kXtxTmemCols = 512;  // two 128 x 256 fp32 accumulators
 constexpr int64_t kXtxMaxTokens = 262144;  // tokens per launch
@@ -325,7 +325,7 @@ static int64_t xtx_tiles(int64_t cols) {
 // of 128 channels (four 32-channel blocks) and one contiguous token slice.
 // Each stage is one TMA tile X[n0:n0+64, c0:c0+128]; it is both MMA operands
 // (A = B: the 128 x 128 tile X_s^T X_s, M = N = 128, K = 16 per instruction,
-// 4 per stage), accumulated in TMEM in chunks of 256 tokens (two 128-column
+// 4 per stage), accumulated in TMEM in chunks of 1024 tokens (two 128-column
 // buffers).  Four epilogue warps read only the diagonal 32x32 sub-blocks
 // (warp quarter q: TMEM lanes 32q.., columns 32q..) and add each chunk into
 // round-to-nearest fp32 totals in registers, as the full X^T X kernel does.
